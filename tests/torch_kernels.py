@@ -114,6 +114,125 @@ class TorchKernels:
             start += n
         return out.reshape(T, heads * head_dim).to(qkv.dtype)
 
+    # ------------------------------------------------------------------ layer norm around sub-layers
+    @staticmethod
+    def _layernorm(x, norm):
+        mean = x.mean(dim=-1, keepdim=True)
+        dev = x - mean
+        y = dev * torch.rsqrt((dev * dev).mean(dim=-1, keepdim=True) + norm.eps) * norm.weight
+        return y + norm.bias if norm.bias is not None else y
+
+    def add_layernorm(self, residual, delta, after, mult, norm, out_dtype):
+        if delta is not None:
+            d = delta.to(torch.float32)
+            residual += mult * (self._layernorm(d, after) if after is not None else d)
+        if norm is None:
+            return None
+        return self._layernorm(residual, norm).to(out_dtype)
+
+    # ------------------------------------------------------------------ latent attention
+    @staticmethod
+    def _rotate(x, positions, inv_freq, rotary_dim):
+        """x [T, ..., D] float32: pairs (i, i + rotary_dim/2) of the first rotary_dim elements."""
+        half = rotary_dim // 2
+        angles = positions.to(torch.float32)[:, None] * inv_freq[None, :]
+        shape = [x.shape[0]] + [1] * (x.dim() - 2) + [half]
+        cos, sin = torch.cos(angles).view(shape), torch.sin(angles).view(shape)
+        out = x.clone()
+        a, b = x[..., :half], x[..., half:rotary_dim]
+        out[..., :half] = a * cos - b * sin
+        out[..., half:rotary_dim] = b * cos + a * sin
+        return out
+
+    def latent_prepare(self, down, batch, q_rank, kv_rank, rot_dim, q_norm, kv_norm, eps, inv_freq, rotary_dim, view,
+                       write, out_dtype):
+        down = down.float()
+        cq = down[:, :q_rank]
+        cq = cq * torch.rsqrt(cq.pow(2).mean(-1, keepdim=True) + eps) * q_norm
+        c = down[:, q_rank:q_rank + kv_rank]
+        c = c * torch.rsqrt(c.pow(2).mean(-1, keepdim=True) + eps) * kv_norm
+        row = c
+        if rot_dim:
+            shared = self._rotate(down[:, q_rank + kv_rank:q_rank + kv_rank + rot_dim], batch.positions, inv_freq, rotary_dim)
+            row = torch.cat([c, shared], dim=-1)
+        if write and view is not None:
+            P = view.page_size
+            pos = batch.positions.long()
+            pages = view.block_table[batch.seg_of_token.long(), pos // P].long()
+            view.rows[pages, pos % P] = row.to(view.rows.dtype)
+        return cq.to(out_dtype)
+
+    def heads_linear(self, x, w):
+        """x [T, H, K] (any strides), w [H, N, K] -> [T, H, N]."""
+        return torch.einsum("thk,hnk->thn", x.float(), w.float()).to(x.dtype)
+
+    def latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim):
+        T, H, R = q_latent.shape
+        out = torch.empty(T, H, R, dtype=torch.float32, device=q_latent.device)
+        P = view.page_size
+        ql = q_latent.float()
+        qr = self._rotate(q_rot.float(), batch.positions, inv_freq, rotary_dim) if q_rot is not None else None
+        start = 0
+        for r, n in enumerate(batch.seg_lens):
+            pos0 = batch.seg_pos0_list[r]
+            ctx = pos0 + n
+            n_pages = -(-ctx // P)
+            rows = view.rows[view.block_table[r, :n_pages].long()].reshape(n_pages * P, -1)[:ctx].float()
+            scores = torch.einsum("thr,sr->hts", ql[start:start + n], rows[:, :R])
+            if qr is not None:
+                scores = scores + torch.einsum("thd,sd->hts", qr[start:start + n], rows[:, R:])
+            scores = scores * scale
+            qpos = torch.arange(pos0, ctx, device=ql.device)[:, None]
+            kpos = torch.arange(ctx, device=ql.device)[None, :]
+            scores = scores.masked_fill(~(kpos <= qpos)[None], float("-inf"))
+            if sinks is not None:
+                full = torch.cat([scores, sinks.view(H, 1, 1).expand(H, n, 1)], dim=-1)
+                weights = torch.softmax(full, dim=-1)[..., :ctx]
+            else:
+                weights = torch.softmax(scores, dim=-1)
+            out[start:start + n] = torch.einsum("hts,sr->thr", weights, rows[:, :R])
+            start += n
+        return out.to(q_latent.dtype)
+
+    def gate_heads(self, out, gate):
+        T, H, V = out.shape
+        o = out.float()
+        if gate is not None:
+            g = torch.sigmoid(gate.float())
+            o = o * (g[:, :, None] if g.shape[1] == H else g.view(T, H, V))
+        return o.reshape(T, H * V).to(out.dtype)
+
+    # ------------------------------------------------------------------ routed experts
+    def route_top(self, x, w_router, experts, top, shared):
+        logits = x.float() @ w_router.t()
+        order = torch.sort(logits[:, :experts], dim=-1, descending=True, stable=True).indices[:, :top]
+        chosen = torch.gather(logits[:, :experts], 1, order)
+        weight = torch.softmax(chosen, dim=-1)
+        gate = torch.sigmoid(logits[:, experts]) if shared else None
+        return order.to(torch.int32), weight, gate
+
+    @staticmethod
+    def _glu_clamped(gate_up, limit, alpha):
+        inter = gate_up.shape[-1] // 2
+        g = gate_up[..., :inter].float().clamp(max=limit)
+        u = gate_up[..., inter:].float().clamp(min=-limit, max=limit)
+        return g * torch.sigmoid(alpha * g) * (u + 1.0)
+
+    def linear_glu_clamped(self, x, w_gate_up, limit, alpha):
+        return self._glu_clamped(self.linear(x, w_gate_up), limit, alpha).to(x.dtype)
+
+    def routed_experts(self, x, choice, weight, w_gate_up, w_down, limit, alpha, shared_out, shared_gate):
+        T, top = choice.shape
+        out = torch.zeros(T, w_down.shape[1], dtype=torch.float32, device=x.device)
+        for t in range(T):
+            for j in range(top):
+                e = int(choice[t, j])
+                hidden = self._glu_clamped(self.linear(x[t:t + 1], w_gate_up[e]), limit, alpha).to(x.dtype)
+                out[t] += weight[t, j] * self.linear(hidden, w_down[e]).float()[0]
+        if shared_out is not None:
+            out += shared_out.float() * shared_gate[:, None]
+        return out
+
     # ------------------------------------------------------------------ sampling
     @staticmethod
     def uniform(seed: int, counter: int) -> float:

@@ -1,10 +1,10 @@
 """Parts that layers are put together from, and the generic decoder that runs them."""
 
-from . import attention, block, embedding, feed_forward, norm, position  # noqa: F401  (they register themselves)
-from .base import (Block, CacheRequest, FeedForward, Mixer, Norm, OutputHead, PagedKV, PagedKVView, Part, PartSpec, PositionEncoding, Runtime,
+from . import attention, block, embedding, feed_forward, latent_attention, norm, position, routed_experts  # noqa: F401  (they register themselves)
+from .base import (Block, CacheRequest, FeedForward, LatentPages, LatentPagesView, PendingDelta, Mixer, Norm, OutputHead, PagedKV, PagedKVView, Part, PartSpec, PositionEncoding, Runtime,
                    SlotState, SlotStateView, StepBatch, TensorSpec, TokenEmbedding, build_part, register_part)
 from .model import DecoderModel, LayerCall, LayerSpec, ModelSpec
 
-__all__ = ["Block", "CacheRequest", "OutputHead", "TokenEmbedding", "FeedForward", "Mixer", "Norm", "PagedKV", "PagedKVView", "Part", "PartSpec", "PositionEncoding",
+__all__ = ["Block", "LatentPages", "LatentPagesView", "PendingDelta", "CacheRequest", "OutputHead", "TokenEmbedding", "FeedForward", "Mixer", "Norm", "PagedKV", "PagedKVView", "Part", "PartSpec", "PositionEncoding",
            "Runtime", "SlotState", "SlotStateView", "StepBatch", "TensorSpec", "build_part", "register_part",
            "DecoderModel", "LayerCall", "LayerSpec", "ModelSpec"]

@@ -90,6 +90,35 @@ class SlotState(CacheRequest):
         return SlotStateView(state=tensors["state"], slots=slots, slot_list=slot_list)
 
 
+@dataclass(frozen=True)
+class LatentPages(CacheRequest):
+    """One vector per token instead of keys and values: `latent` numbers from which a mixer makes every
+    head's key and value, followed by `extra` numbers that are kept as they are (a rotated key part that all
+    heads share). A page holds page_size such rows, contiguous."""
+
+    latent: int
+    extra: int = 0
+    window: Optional[int] = None
+    paged = True
+
+    def storage(self, page_size: int):
+        return {"rows": ((page_size, self.latent + self.extra), None)}
+
+    def view(self, tensors, *, block_table, page_size, **_):
+        return LatentPagesView(rows=tensors["rows"], block_table=block_table, page_size=page_size,
+                               latent=self.latent, extra=self.extra, window=self.window)
+
+
+@dataclass
+class LatentPagesView:
+    rows: torch.Tensor          # [num_pages, page_size, latent + extra]
+    block_table: torch.Tensor   # int32 [segments, pages_per_request]
+    page_size: int
+    latent: int
+    extra: int
+    window: Optional[int]
+
+
 @dataclass
 class PagedKVView:
     """One cache unit of a paged group as a mixer sees it during a step."""
@@ -172,6 +201,15 @@ class DeferredNorm:
 
     def materialize(self):
         return self._materialize()
+
+
+class PendingDelta:
+    """A sub-layer output that is not in the residual stream yet and needs more than an addition to get
+    there (a norm of its own, a multiplier). A block that knows the kind takes it into its first norm's
+    kernel; for everything else `settle(residual)` adds it in place."""
+
+    def settle(self, residual) -> None:
+        raise NotImplementedError
 
 
 class _Added:

@@ -15,7 +15,7 @@ tensors only, as before.
 
 from __future__ import annotations
 
-from .base import ADDED, Block, DeferredNorm, register_part
+from .base import ADDED, Block, DeferredNorm, PendingDelta, register_part
 
 
 def _normed(norm, consumer, x, delta):
@@ -57,3 +57,61 @@ class PreNormBlock(Block):
 
 
 register_part("block", "pre_norm", PreNormBlock)
+
+
+class NormedDelta(PendingDelta):
+    """A sub-layer's output that still has to pass a norm of its own and a multiplier before it joins the stream."""
+
+    def __init__(self, tensor, norm, mult):
+        self.tensor, self.norm, self.mult = tensor, norm, mult
+
+    def settle(self, residual):
+        self.norm.join(residual, self.tensor, self.mult)
+
+
+class SandwichBlock(Block):
+    """A norm before and a norm after each sub-layer, and a multiplier m on what joins the stream:
+        x += m * post1(mixer(norm1(x)));  x += m * post2(ff(norm2(x))).
+    The stream is float32. A sub-layer's output is not added at once: the kernel of the next norm before a
+    sub-layer first runs the pending norm-after, adds, and then norms the sum, reading and writing the stream
+    once (the second sub-layer's output travels to the next block, or to the model's end, as a NormedDelta).
+    Norm parts need `forward_add(x, delta, after=, mult=)` and `join` (kind `layernorm`)."""
+
+    slots = {"norm1": "norm", "mixer": "mixer", "post1": "norm", "norm2": "norm", "feed_forward": "feed_forward",
+             "post2": "norm"}
+    takes_pending = True
+
+    def __init__(self, norm1, mixer, post1, norm2=None, feed_forward=None, post2=None, residual_mult: float = 1.0):
+        self.norm1, self.mixer, self.post1 = norm1, mixer, post1
+        self.norm2, self.feed_forward, self.post2 = norm2, feed_forward, post2
+        self.residual_mult = float(residual_mult)
+
+    @staticmethod
+    def _normed(norm, x, delta):
+        if isinstance(delta, NormedDelta):
+            return norm.forward_add(x, delta.tensor, after=delta.norm, mult=delta.mult)
+        if isinstance(delta, PendingDelta):
+            delta.settle(x)
+            delta = None
+        return norm.forward_add(x, delta)
+
+    def forward(self, x, delta, batch, cache, write_cache=True):
+        h = self._normed(self.norm1, x, delta)
+        pending = NormedDelta(self.mixer.forward(h, batch, cache, write_cache), self.post1, self.residual_mult)
+        if self.feed_forward is None:
+            return x, pending
+        h = self._normed(self.norm2, x, pending)
+        return x, NormedDelta(self.feed_forward.forward(h, batch), self.post2, self.residual_mult)
+
+
+class SandwichMixerBlock(SandwichBlock):
+    """The same block for a layer without a feed-forward: x += m * post1(mixer(norm1(x)))."""
+
+    slots = {"norm1": "norm", "mixer": "mixer", "post1": "norm"}
+
+    def graph_safe(self) -> bool:
+        return bool(getattr(self.mixer, "graph_safe", False))
+
+
+register_part("block", "sandwich", SandwichBlock)
+register_part("block", "sandwich_mixer_only", SandwichMixerBlock)

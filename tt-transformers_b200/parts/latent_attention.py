@@ -1,0 +1,102 @@
+"""Attention over a cached low-rank latent.
+
+Per token the cache holds one vector: the latent c (`kv_rank` numbers, RMS-normed) and, where the mixer has
+a rotated part, `rot_dim` more numbers, one rotated key part that all heads share. Keys and values of a
+head are linear in c (k = W_uk c, v = W_uv c), so neither is ever materialised: the head's query is carried
+into the latent space, q' = W_uk^T q, the scores are q' . c (+ q_rot . k_rot), the weighted sum of the
+latents comes back through W_uv. Per step and layer the cache is read once, whatever the number of heads.
+
+    c_q = RMS(W_dq h) * g_q;  q = W_uq c_q  (per head [dim | rot_dim])
+    [c_raw | k_rot] = W_dkv h;  c = RMS(c_raw) * g_kv
+    score_h(i, j) = (q_h,plain(i) . W_uk,h c(j) + R(i) q_h,rot(i) . R(j) k_rot(j)) * scale,  j <= i
+    weights: softmax over j, with exp(sink_h) added to the denominator where the mixer has sinks
+    o_h(i) = W_uv,h sum_j weight(i, j) c(j);  out = W_o (o * sigmoid(W_g h))
+
+Options, all parameters: `rot_dim` 0 leaves positions out altogether; `sink` adds one learned number per
+head to the softmax's denominator (it has no key and no value and is not scaled); `gate` is "element"
+(one gate number per output element of the heads), "head" (one per head) or None. Norms, rotation angles,
+scores and softmax are float32. The down projections of one input (W_dq, W_dkv, W_g) run as one product.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .base import LatentPages, Mixer, PositionEncoding, TensorSpec, register_part
+
+
+class LatentAttention(Mixer):
+    graph_safe = True
+
+    def __init__(self, width: int, heads: int, dim: int, vdim: int, q_rank: int, kv_rank: int, scale: float, eps: float,
+                 prefix: str, rot_dim: int = 0, sink: bool = False, gate: Optional[str] = None,
+                 position: Optional[PositionEncoding] = None, window: Optional[int] = None):
+        self.width, self.heads, self.dim, self.vdim = int(width), int(heads), int(dim), int(vdim)
+        self.q_rank, self.kv_rank, self.rot_dim = int(q_rank), int(kv_rank), int(rot_dim)
+        self.scale, self.eps, self.prefix = float(scale), float(eps), prefix
+        self.sink, self.gate, self.position, self.window = bool(sink), gate, position, window
+        if gate not in (None, "element", "head"):
+            raise ValueError(f"gate must be 'element', 'head' or None, got {gate!r}")
+        if self.rot_dim and (position is None or not hasattr(position, "rotary_dim")):
+            raise ValueError("a mixer with a rotated part needs a rotary position encoding")
+        if self.rot_dim and getattr(position, "interleaved", False):
+            raise ValueError("the rotated part pairs element i with i + dims/2; neighbouring pairs are not built")
+        if self.rot_dim and position.rotary_dim > self.rot_dim:
+            raise ValueError(f"the rotation covers {position.rotary_dim} elements, the rotated part has {self.rot_dim}")
+
+    @property
+    def gate_rows(self) -> int:
+        return {None: 0, "element": self.heads * self.vdim, "head": self.heads}[self.gate]
+
+    def tensor_specs(self):
+        p, H = self.prefix, self.heads
+        specs = [TensorSpec(p + "dq", (self.q_rank, self.width)), TensorSpec(p + "dq.norm", (self.q_rank,)),
+                 TensorSpec(p + "uq", (H * (self.dim + self.rot_dim), self.q_rank)),
+                 TensorSpec(p + "dkv", (self.kv_rank + self.rot_dim, self.width)),
+                 TensorSpec(p + "dkv.norm", (self.kv_rank,)),
+                 TensorSpec(p + "uk", (H * self.dim, self.kv_rank)), TensorSpec(p + "uv", (H * self.vdim, self.kv_rank)),
+                 TensorSpec(p + "o", (self.width, H * self.vdim))]
+        if self.sink:
+            specs.append(TensorSpec(p + "sink", (H,)))
+        if self.gate:
+            specs.append(TensorSpec(p + "g", (self.gate_rows, self.width)))
+        return specs
+
+    def bind(self, tensors, runtime):
+        super().bind(tensors, runtime)
+        p, H = self.prefix, self.heads
+        down = [tensors[p + "dq"], tensors[p + "dkv"]] + ([tensors[p + "g"]] if self.gate else [])
+        self.w_down = runtime.matrix(torch.cat(down, 0))         # [q_rank + kv_rank + rot_dim + gate rows, width]
+        self.w_uq = runtime.matrix(tensors[p + "uq"])
+        # per head, the matrix that carries a query into the latent space: (W_uk,h)^T as [kv_rank, dim]
+        self.w_uk_t = runtime.matrix(tensors[p + "uk"].view(H, self.dim, self.kv_rank).transpose(1, 2))
+        self.w_uv = runtime.matrix(tensors[p + "uv"].view(H, self.vdim, self.kv_rank))
+        self.w_o = runtime.matrix(tensors[p + "o"])
+        f32 = dict(device=runtime.device, dtype=torch.float32)
+        self.q_norm = tensors[p + "dq.norm"].to(**f32).contiguous()
+        self.kv_norm = tensors[p + "dkv.norm"].to(**f32).contiguous()
+        self.sinks = tensors[p + "sink"].to(**f32).contiguous() if self.sink else None
+
+    def cache_request(self):
+        return LatentPages(self.kv_rank, self.rot_dim, self.window)
+
+    def forward(self, x, batch, cache, write_cache=True):
+        k = self.runtime.kernels
+        H, D, R, rot = self.heads, self.dim, self.kv_rank, self.rot_dim
+        inv_freq, rotary_dim = self.position.rotation() if rot else (None, 0)
+        down = k.linear(x, self.w_down, out_dtype=torch.float32)
+        # the query latent, normed; the key/value latent, normed, and the rotated key part into the pages
+        c_q = k.latent_prepare(down, batch, self.q_rank, R, rot, self.q_norm, self.kv_norm, self.eps, inv_freq, rotary_dim,
+                               cache, write_cache, self.runtime.dtype)
+        q = k.linear(c_q, self.w_uq).view(-1, H, D + rot)
+        q_latent = k.heads_linear(q[:, :, :D], self.w_uk_t)                       # [T, H, R]
+        mixed = k.latent_attention(q_latent, q[:, :, D:] if rot else None, batch, cache, self.scale, self.sinks,
+                                   inv_freq, rotary_dim)                           # [T, H, R]
+        out = k.heads_linear(mixed, self.w_uv)                                      # [T, H, vdim]
+        gate = down[:, self.q_rank + R + rot:] if self.gate else None
+        return k.linear(k.gate_heads(out, gate), self.w_o)
+
+
+register_part("mixer", "latent_attention", LatentAttention)

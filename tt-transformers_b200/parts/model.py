@@ -17,7 +17,7 @@ from typing import Dict, List, Optional
 
 import torch
 
-from .base import ADDED, Block, DeferredNorm, PartSpec, Runtime, StepBatch, TensorSpec, build_part, block_factory
+from .base import ADDED, Block, DeferredNorm, PartSpec, PendingDelta, Runtime, StepBatch, TensorSpec, build_part, block_factory
 
 
 def _block_graph_safe(block) -> bool:
@@ -33,13 +33,15 @@ class LayerSpec:
     more parts, say norms after its sub-layers, names more), and the position encoding handed to
     the layer's mixer as `position`."""
 
-    __slots__ = ("block", "position", "parts")
+    __slots__ = ("block", "position", "parts", "block_params")
 
-    def __init__(self, block: str = "pre_norm", position: Optional[PartSpec] = None, **parts: PartSpec):
+    def __init__(self, block: str = "pre_norm", position: Optional[PartSpec] = None, block_params: Optional[dict] = None,
+                 **parts: PartSpec):
         for name, spec in parts.items():
             if not isinstance(spec, PartSpec):
                 raise TypeError(f"LayerSpec: part {name!r} must be a PartSpec, got {type(spec).__name__}")
         self.block, self.position, self.parts = block, position, dict(parts)
+        self.block_params = dict(block_params or {})     # constants of the block kind itself (a residual multiplier)
 
     def __getattr__(self, name):                 # spec.mixer, spec.norm1, ... read like fields
         parts = object.__getattribute__(self, "parts")
@@ -109,7 +111,7 @@ class DecoderModel:
                 if category == "mixer" and position is not None:
                     part_spec = PartSpec(part_spec.kind, dict(part_spec.params, position=position))
                 built[name] = build_part(category, part_spec)
-            self.layers.append(factory(**built))
+            self.layers.append(factory(**built, **ls.block_params))
         self.positions = list(positions.values())
         for i, call in enumerate(spec.order):
             if not 0 <= call.layer < len(self.layers):
@@ -188,6 +190,9 @@ class DecoderModel:
             owner = i if call.cache_of is None else call.cache_of
             block = self.layers[call.layer]
             view = cache.view(owner, batch)
+            if isinstance(delta, PendingDelta) and not getattr(block, "takes_pending", False):
+                delta.settle(x)                   # a block kind that does not know it: plain addition first
+                delta = None
             if getattr(block, "takes_next_norm", False):
                 # the norm that will run on this block's result, if what follows it can take it half done
                 if i + 1 < len(order):
@@ -204,6 +209,9 @@ class DecoderModel:
                 if delta is ADDED or isinstance(delta, DeferredNorm):
                     delta = None
                 x, delta = block.forward(x, delta, batch, view, write_cache=call.cache_of is None)
+        if isinstance(delta, PendingDelta):
+            delta.settle(x)
+            delta = None
         if batch.num_wanted == 0:
             return torch.empty(0, self.spec.vocab_size, dtype=torch.float32, device=x.device)
         if isinstance(delta, DeferredNorm) and delta.made_for is self.final_norm and batch.wants_every_row:

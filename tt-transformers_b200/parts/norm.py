@@ -7,6 +7,8 @@ as well and is written back to the residual stream.
 
 from __future__ import annotations
 
+import torch
+
 from .base import ADDED, DeferredNorm, Norm, TensorSpec, register_part
 
 
@@ -44,3 +46,39 @@ class RMSNorm(Norm):
 
 
 register_part("norm", "rmsnorm", RMSNorm)
+
+
+class LayerNorm(Norm):
+    """y = (x - mean) / sqrt(var + eps) * w + b with the variance as the mean squared deviation; mean,
+    variance and scaling in float32. `bias_name` None: no bias. Used before a sub-layer like RMSNorm
+    (`forward_add`), and after one by blocks that norm a sub-layer's output before it joins the stream
+    (`after`)."""
+
+    def __init__(self, width: int, eps: float, weight_name: str, bias_name: str = None):
+        self.width, self.eps, self.weight_name, self.bias_name = int(width), float(eps), weight_name, bias_name
+
+    def tensor_specs(self):
+        specs = [TensorSpec(self.weight_name, (self.width,))]
+        if self.bias_name is not None:
+            specs.append(TensorSpec(self.bias_name, (self.width,)))
+        return specs
+
+    def bind(self, tensors, runtime):
+        super().bind(tensors, runtime)
+        self.weight = tensors[self.weight_name].to(device=runtime.device, dtype=torch.float32).contiguous()
+        self.bias = None
+        if self.bias_name is not None:
+            self.bias = tensors[self.bias_name].to(device=runtime.device, dtype=torch.float32).contiguous()
+
+    def forward_add(self, residual, delta, after: "LayerNorm" = None, mult: float = 1.0):
+        """residual += mult * (after(delta) if `after` else delta), then this norm of the residual."""
+        if delta is ADDED or isinstance(delta, DeferredNorm):
+            delta = None
+        return self.runtime.kernels.add_layernorm(residual, delta, after, mult, self, self.runtime.dtype)
+
+    def join(self, residual, delta, mult: float = 1.0):
+        """residual += mult * norm(delta): this norm applied to a sub-layer's output on its way into the stream."""
+        self.runtime.kernels.add_layernorm(residual, delta, self, mult, None, self.runtime.dtype)
+
+
+register_part("norm", "layernorm", LayerNorm)

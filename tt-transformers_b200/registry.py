@@ -1,4 +1,4 @@
-"""One registry from the architecture's name (config.json `architectures[0]`) to its model.
+"""One registry from the architecture's name (config.json `architectures[0]`, or `architecture`) to its model.
 
 An architecture is three functions in one module: `load_config(dict)` gives the typed
 configuration, `model_spec(config)` the ModelSpec, `ignorable(config, tensor_name)` says
@@ -27,6 +27,7 @@ class Architecture:
 
 _ARCHITECTURES: Dict[str, Union[str, Architecture]] = {
     "LlamaForCausalLM": "tt_transformers_b200.models.llama",
+    "Bozavik": "tt_transformers_b200.models.bozavik",
 }
 
 
@@ -50,6 +51,9 @@ def get_architecture(name: str) -> Architecture:
 
 
 def architecture_of(config_dict: dict) -> str:
+    single = config_dict.get("architecture")
+    if isinstance(single, str) and "architectures" not in config_dict:
+        return single                                  # configurations that name their one class under 'architecture'
     archs = config_dict.get("architectures")
     if not isinstance(archs, list) or not archs or not isinstance(archs[0], str):
         from .config.base import ConfigError
