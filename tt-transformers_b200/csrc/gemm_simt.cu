@@ -25,7 +25,10 @@ __device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
 template <typename TA, typename TC, bool VEC>
 __global__ void __launch_bounds__(GS_THREADS)
 gemm_simt_kernel(const TA* __restrict__ A, const TA* __restrict__ W, TC* __restrict__ C, int M, int N, int K,
-                 int lda, int ldw, int ldc) {
+                 int lda, int ldw, int ldc, long long batch_a = 0, long long batch_w = 0, long long batch_c = 0) {
+    A += (size_t)blockIdx.z * batch_a;       // one product per blockIdx.z (a single product: one z, strides 0)
+    W += (size_t)blockIdx.z * batch_w;
+    C += (size_t)blockIdx.z * batch_c;
     __shared__ float As[GS_BK][GS_BM + 4];
     __shared__ float Ws[GS_BK][GS_BN + 4];
     const int m0 = blockIdx.y * GS_BM, n0 = blockIdx.x * GS_BN;
@@ -97,6 +100,31 @@ TTB_EXPORT int ttb_gemm_simt(const void* A, const void* W, void* C, int in_dtype
     do {                                                                                                           \
         if (vec) gemm_simt_kernel<TA, TC, true><<<grid, GS_THREADS, 0, stream>>>((const TA*)A, (const TA*)W, (TC*)C, M, N, K, lda, ldw, ldc); \
         else gemm_simt_kernel<TA, TC, false><<<grid, GS_THREADS, 0, stream>>>((const TA*)A, (const TA*)W, (TC*)C, M, N, K, lda, ldw, ldc);    \
+    } while (0)
+    if (in_dtype == TTB_DTYPE_F32 && out_dtype == TTB_DTYPE_F32) GS_LAUNCH(float, float);
+    else if (in_dtype == TTB_DTYPE_BF16 && out_dtype == TTB_DTYPE_BF16) GS_LAUNCH(__nv_bfloat16, __nv_bfloat16);
+    else if (in_dtype == TTB_DTYPE_BF16 && out_dtype == TTB_DTYPE_F32) GS_LAUNCH(__nv_bfloat16, float);
+    else return TTB_ERR_UNSUPPORTED;
+#undef GS_LAUNCH
+    return ttb_launch_status();
+}
+
+// `batch` products at once: product b reads A + b * batch_a (rows lda apart), W + b * batch_w, and writes
+// C + b * batch_c, all strides in elements. Per-head products (x[t, h, :] times W[h]) are this with batch_a the
+// head stride of x and lda its token stride.
+TTB_EXPORT int ttb_gemm_simt_batched(const void* A, const void* W, void* C, int in_dtype, int out_dtype, int batch, int M,
+                                     int N, int K, int lda, int ldw, int ldc, long long batch_a, long long batch_w,
+                                     long long batch_c, cudaStream_t stream) {
+    if (M == 0 || N == 0 || batch == 0) return TTB_OK;
+    if (!A || !W || !C || K < 1) return TTB_ERR_ARGUMENT;
+    dim3 grid((N + GS_BN - 1) / GS_BN, (M + GS_BM - 1) / GS_BM, batch);
+    if (grid.y > 65535 || batch > 65535) return TTB_ERR_UNSUPPORTED;
+    const bool vec = (K % 4 == 0) && (lda % 4 == 0) && (ldw % 4 == 0) && (batch_a % 4 == 0) && (batch_w % 4 == 0) &&
+                     aligned16(A) && aligned16(W);
+#define GS_LAUNCH(TA, TC)                                                                                          \
+    do {                                                                                                           \
+        if (vec) gemm_simt_kernel<TA, TC, true><<<grid, GS_THREADS, 0, stream>>>((const TA*)A, (const TA*)W, (TC*)C, M, N, K, lda, ldw, ldc, batch_a, batch_w, batch_c); \
+        else gemm_simt_kernel<TA, TC, false><<<grid, GS_THREADS, 0, stream>>>((const TA*)A, (const TA*)W, (TC*)C, M, N, K, lda, ldw, ldc, batch_a, batch_w, batch_c);    \
     } while (0)
     if (in_dtype == TTB_DTYPE_F32 && out_dtype == TTB_DTYPE_F32) GS_LAUNCH(float, float);
     else if (in_dtype == TTB_DTYPE_BF16 && out_dtype == TTB_DTYPE_BF16) GS_LAUNCH(__nv_bfloat16, __nv_bfloat16);

@@ -1,0 +1,87 @@
+// Layer norm with weight and bias around sub-layers, fused with the residual add between them.
+//   residual += mult * after(delta)      (after: a layer norm of the sub-layer's output; absent: delta itself)
+//   out = norm(residual)                 (norm: the layer norm before the next sub-layer; absent: nothing is written)
+// y = (x - mean) / sqrt(var + eps) * w + b, var = mean((x - mean)^2); the residual stream, both means, both
+// variances and the scaling are float32. One block per row; the row stays in shared memory between the passes, so
+// the variance is the mean of squared deviations from the exact mean (no E[x^2] - E[x]^2 cancellation).
+#include "common.cuh"
+
+#define LN_THREADS 256
+
+__device__ __forceinline__ void ln_stats(const float* row, int width, float eps, float* scratch, float& mean, float& rstd) {
+    float s = 0.f;
+    for (int c = threadIdx.x; c < width; c += blockDim.x) s += row[c];
+    mean = block_sum(s, scratch) / (float)width;
+    float q = 0.f;
+    for (int c = threadIdx.x; c < width; c += blockDim.x) {
+        const float d = row[c] - mean;
+        q += d * d;
+    }
+    rstd = rsqrtf(block_sum(q, scratch) / (float)width + eps);
+}
+
+template <typename TD, typename TO>
+__global__ void __launch_bounds__(LN_THREADS)
+add_layernorm_kernel(float* __restrict__ residual, const TD* __restrict__ delta, int ld_delta,
+                     const float* __restrict__ after_w, const float* __restrict__ after_b, float after_eps, float mult,
+                     const float* __restrict__ norm_w, const float* __restrict__ norm_b, float norm_eps,
+                     TO* __restrict__ out, int width) {
+    extern __shared__ float row[];
+    __shared__ float scratch[32];
+    pdl_wait();
+    pdl_launch_dependents();
+    float* res = residual + (size_t)blockIdx.x * width;
+    if (delta != nullptr) {
+        const TD* d = delta + (size_t)blockIdx.x * ld_delta;
+        for (int c = threadIdx.x; c < width; c += blockDim.x) row[c] = to_float(d[c]);
+        __syncthreads();
+        float mean = 0.f, rstd = 1.f;
+        if (after_w != nullptr) ln_stats(row, width, after_eps, scratch, mean, rstd);
+        __syncthreads();
+        for (int c = threadIdx.x; c < width; c += blockDim.x) {
+            float y = row[c];
+            if (after_w != nullptr) y = (y - mean) * rstd * after_w[c] + (after_b != nullptr ? after_b[c] : 0.f);
+            const float v = res[c] + mult * y;
+            res[c] = v;
+            row[c] = v;
+        }
+    } else {
+        for (int c = threadIdx.x; c < width; c += blockDim.x) row[c] = res[c];
+    }
+    if (norm_w == nullptr) return;
+    __syncthreads();
+    float mean, rstd;
+    ln_stats(row, width, norm_eps, scratch, mean, rstd);
+    TO* o = out + (size_t)blockIdx.x * width;
+    for (int c = threadIdx.x; c < width; c += blockDim.x)
+        o[c] = from_float<TO>((row[c] - mean) * rstd * norm_w[c] + (norm_b != nullptr ? norm_b[c] : 0.f));
+}
+
+// delta: null, float32 or bfloat16 [rows, ld_delta]; weights and biases float32; out: float32 or bfloat16 (null with norm_w null).
+TTB_EXPORT int ttb_add_layernorm(float* residual, const void* delta, int delta_dtype, int ld_delta, const float* after_w,
+                                 const float* after_b, float after_eps, float mult, const float* norm_w,
+                                 const float* norm_b, float norm_eps, void* out, int out_dtype, int rows, int width,
+                                 cudaStream_t stream) {
+    if (rows == 0) return TTB_OK;
+    if (!residual || width < 1 || (norm_w && !out)) return TTB_ERR_ARGUMENT;
+    const size_t smem = (size_t)width * sizeof(float);
+    if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
+#define LN_LAUNCH(TD, TO)                                                                                            \
+    do {                                                                                                             \
+        if (smem > 48 * 1024)                                                                                        \
+            cudaFuncSetAttribute(add_layernorm_kernel<TD, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+        ttb_launch(add_layernorm_kernel<TD, TO>, rows, LN_THREADS, smem, stream, residual, (const TD*)delta, ld_delta,    \
+                   after_w, after_b, after_eps, mult, norm_w, norm_b, norm_eps, (TO*)out, width);                    \
+    } while (0)
+    const bool d_bf16 = delta && delta_dtype == TTB_DTYPE_BF16;
+    if (delta && delta_dtype != TTB_DTYPE_BF16 && delta_dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
+    if (out_dtype == TTB_DTYPE_BF16) {
+        if (d_bf16) LN_LAUNCH(__nv_bfloat16, __nv_bfloat16); else LN_LAUNCH(float, __nv_bfloat16);
+    } else if (out_dtype == TTB_DTYPE_F32) {
+        if (d_bf16) LN_LAUNCH(__nv_bfloat16, float); else LN_LAUNCH(float, float);
+    } else {
+        return TTB_ERR_UNSUPPORTED;
+    }
+#undef LN_LAUNCH
+    return ttb_launch_status();
+}

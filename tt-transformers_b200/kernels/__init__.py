@@ -93,7 +93,9 @@ class CudaKernels:
                      "ttb_gemm_tcgen05", "ttb_paged_attention_tcgen05", "ttb_attention_tcgen05_supports",
                      "ttb_attention_tcgen05_tile_rows", "ttb_attention_merge", "ttb_gemv_qkv_rope",
                      "ttb_gemm_skinny_tcgen05", "ttb_gemm_skinny_tcgen05_rows", "ttb_softcap", "ttb_sample_scratch_bytes",
-                     "ttb_gemv_ring", "ttb_gemm_skinny_tcgen05_qkv_rope"):
+                     "ttb_gemv_ring", "ttb_gemm_skinny_tcgen05_qkv_rope", "ttb_add_layernorm", "ttb_latent_prepare",
+                     "ttb_latent_attention_generic", "ttb_gate_heads", "ttb_gemm_simt_batched", "ttb_route_top",
+                     "ttb_moe_align", "ttb_moe_group_gemm", "ttb_moe_combine", "ttb_glu_clamped"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -579,6 +581,165 @@ class CudaKernels:
             "paged_attention_mma")
         if splits > 1:
             self.launches += 1
+
+    # ------------------------------------------------------------------ layer norm around sub-layers
+    def add_layernorm(self, residual, delta, after, mult, norm, out_dtype):
+        """residual += mult * (after(delta) if after else delta), in place and in float32; then norm(residual) in
+        out_dtype (None when norm is None). `after` and `norm` are layer-norm parts (weight, bias or None, eps)."""
+        rows, width = residual.shape
+        if residual.dtype != torch.float32 or not residual.is_contiguous():
+            raise KernelError("the residual stream is float32 and contiguous")
+        if delta is not None and (delta.shape != residual.shape or delta.stride(1) != 1):
+            raise KernelError("add_layernorm: delta must have the residual's shape")
+        out = torch.empty(rows, width, dtype=out_dtype, device=self.device) if norm is not None else None
+        self._check(self.lib.ttb_add_layernorm(
+            self._p(residual), self._p(delta), _dtype_code(delta.dtype) if delta is not None else 0,
+            delta.stride(0) if delta is not None else 0,
+            self._p(after.weight if after is not None else None), self._p(after.bias if after is not None else None),
+            ctypes.c_float(after.eps if after is not None else 0.0), ctypes.c_float(mult),
+            self._p(norm.weight if norm is not None else None), self._p(norm.bias if norm is not None else None),
+            ctypes.c_float(norm.eps if norm is not None else 0.0), self._p(out), _dtype_code(out_dtype), rows, width,
+            self._stream()), "add_layernorm")
+        return out
+
+    # ------------------------------------------------------------------ latent attention
+    def latent_prepare(self, down, batch, q_rank, kv_rank, rot_dim, q_norm, kv_norm, eps, inv_freq, rotary_dim, view,
+                       write, out_dtype):
+        """down: float32 [T, >= q_rank + kv_rank + rot_dim]. Returns the RMS-normed query latent [T, q_rank]; writes
+        the RMS-normed key/value latent and the rotated shared key part into the tokens' page rows."""
+        tokens = down.shape[0]
+        if down.dtype != torch.float32 or down.stride(1) != 1:
+            raise KernelError("latent_prepare: the down projection must be float32, contiguous along its columns")
+        write = bool(write and view is not None)
+        if write and (view.rows.dtype != out_dtype or not view.rows.is_contiguous()):
+            raise KernelError("latent_prepare: the cache rows must be contiguous and of the compute dtype")
+        cq = torch.empty(tokens, q_rank, dtype=out_dtype, device=self.device)
+        self._check(self.lib.ttb_latent_prepare(
+            self._p(down), down.stride(0), q_rank, kv_rank, rot_dim, self._p(q_norm), self._p(kv_norm),
+            ctypes.c_float(eps), self._p(inv_freq), int(rotary_dim), self._p(batch.positions), self._p(batch.seg_of_token),
+            self._p(cq), self._p(view.rows if write else None), _dtype_code(out_dtype),
+            self._p(view.block_table if write else None), view.block_table.shape[1] if write else 0,
+            view.page_size if write else 1, view.rows.shape[0] if write else 0, 1 if write else 0, tokens,
+            self._p(self.status), self._stream()), "latent_prepare")
+        return cq
+
+    HEADS_LIBRARY_ROWS = 32      # per-head bfloat16 products with at least this many rows go to the library's batched product
+
+    def heads_linear(self, x, w):
+        """x [T, H, K] (any token and head strides) times w [H, N, K], head by head -> [T, H, N] (a view that may
+        be strided; its last axis is contiguous)."""
+        T, H, K = x.shape
+        N = w.shape[1]
+        if w.shape[0] != H or w.shape[2] != K or x.dtype != w.dtype or x.stride(2) != 1 or not w.is_contiguous():
+            raise KernelError(f"heads_linear: x {tuple(x.shape)} does not match w {tuple(w.shape)}")
+        if x.dtype == torch.bfloat16 and T >= self.HEADS_LIBRARY_ROWS:
+            return torch.bmm(x.transpose(0, 1), w.transpose(1, 2)).transpose(0, 1)       # library product (cuBLAS)
+        out = torch.empty(T, H, N, dtype=x.dtype, device=self.device)
+        self._check(self.lib.ttb_gemm_simt_batched(
+            self._p(x), self._p(w), self._p(out), _dtype_code(x.dtype), _dtype_code(x.dtype), H, T, N, K, x.stride(0), K,
+            H * N, ctypes.c_longlong(x.stride(1)), ctypes.c_longlong(N * K), ctypes.c_longlong(N), self._stream()),
+            "heads_linear")
+        return out
+
+    def latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim):
+        """q_latent [T, H, latent], q_rot [T, H, extra] or None (rotated here by the tokens' positions); the cache
+        rows hold [latent | extra] per token. Returns the weighted sums of the latents [T, H, latent]."""
+        T, H, R = q_latent.shape
+        if R != view.latent or q_latent.dtype != view.rows.dtype or q_latent.stride(2) != 1:
+            raise KernelError("latent_attention: the queries do not fit the cache rows")
+        if (q_rot is None) != (view.extra == 0) or (q_rot is not None and (q_rot.shape[2] != view.extra or q_rot.stride(2) != 1)):
+            raise KernelError("latent_attention: the rotated query part does not fit the cache rows")
+        out = torch.empty(T, H, R, dtype=q_latent.dtype, device=self.device)
+        self._check(self.lib.ttb_latent_attention_generic(
+            self._p(q_latent), ctypes.c_longlong(q_latent.stride(0)), ctypes.c_longlong(q_latent.stride(1)),
+            self._p(q_rot), ctypes.c_longlong(q_rot.stride(0) if q_rot is not None else 0),
+            ctypes.c_longlong(q_rot.stride(1) if q_rot is not None else 0), self._p(out), _dtype_code(q_latent.dtype),
+            self._p(batch.positions), self._p(batch.seg_of_token), self._p(view.rows), self._p(view.block_table),
+            view.block_table.shape[1], view.page_size, T, H, R, view.extra, ctypes.c_float(scale), self._p(sinks),
+            self._p(inv_freq), int(rotary_dim), int(view.window or 0), view.rows.shape[0], self._p(self.status),
+            self._stream()), "latent_attention")
+        return out
+
+    def gate_heads(self, out, gate):
+        """out [T, H, V] (any token and head strides) times sigmoid(gate), gate float32 [T, H] or [T, H * V] or
+        None -> contiguous [T, H * V]."""
+        T, H, V = out.shape
+        if out.stride(2) != 1:
+            raise KernelError("gate_heads: the last axis must be contiguous")
+        per_head = 0
+        if gate is not None:
+            if gate.dtype != torch.float32 or gate.stride(1) != 1 or gate.shape[1] not in (H, H * V):
+                raise KernelError("gate_heads: gate must be float32 [T, heads] or [T, heads * vdim]")
+            per_head = 1 if gate.shape[1] == H and V != 1 else 0
+        res = torch.empty(T, H * V, dtype=out.dtype, device=self.device)
+        self._check(self.lib.ttb_gate_heads(
+            self._p(out), ctypes.c_longlong(out.stride(0)), ctypes.c_longlong(out.stride(1)), self._p(gate),
+            gate.stride(0) if gate is not None else 0, per_head, self._p(res), _dtype_code(out.dtype), T, H, V,
+            self._stream()), "gate_heads")
+        return res
+
+    # ------------------------------------------------------------------ routed experts
+    def route_top(self, x, w_router, experts, top, shared):
+        """Float32 router: the `top` experts with the largest logits per token and the softmax over their logits;
+        with `shared`, row `experts` of w_router gives sigmoid(w . x) per token. -> (int32 [T, top], float32 [T, top],
+        float32 [T] or None)."""
+        T, width = x.shape
+        if w_router.dtype != torch.float32 or w_router.shape != (experts + (1 if shared else 0), width) or x.stride(1) != 1:
+            raise KernelError("route_top: the router's matrix must be float32 [experts (+ 1), width]")
+        choice = torch.empty(T, top, dtype=torch.int32, device=self.device)
+        weight = torch.empty(T, top, dtype=torch.float32, device=self.device)
+        gate = torch.empty(T, dtype=torch.float32, device=self.device) if shared else None
+        self._check(self.lib.ttb_route_top(self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(w_router), T, width,
+                                           experts, top, 1 if shared else 0, self._p(choice), self._p(weight),
+                                           self._p(gate), self._stream()), "route_top")
+        return choice, weight, gate
+
+    def glu_clamped(self, gate_up, limit, alpha):
+        rows, two = gate_up.shape
+        out = torch.empty(rows, two // 2, dtype=gate_up.dtype, device=self.device)
+        if not gate_up.is_contiguous():
+            raise KernelError("glu_clamped: the product must be contiguous")
+        self._check(self.lib.ttb_glu_clamped(self._p(gate_up), self._p(out), _dtype_code(gate_up.dtype), rows, two // 2,
+                                             ctypes.c_float(limit), ctypes.c_float(alpha), self._stream()), "glu_clamped")
+        return out
+
+    def linear_glu_clamped(self, x, w_gate_up, limit, alpha):
+        """g' * sigmoid(alpha g') * (u' + 1) with g' = min(x Wg^T, limit), u' = clamp(x Wu^T, -limit, limit), for
+        w_gate_up = [Wg; Wu] stacked along the rows."""
+        return self.glu_clamped(self.linear(x, w_gate_up), limit, alpha)
+
+    def routed_experts(self, x, choice, weight, w_gate_up, w_down, limit, alpha, shared_out, shared_gate):
+        """x [T, width]; choice, weight [T, top]; w_gate_up [E, 2 inter, width]; w_down [E, width, inter] ->
+        float32 [T, width]: sum_j weight[t, j] * expert_choice[t, j](x[t]) (+ shared_gate[t] * shared_out[t])."""
+        T, width = x.shape
+        E, two_inter, _ = w_gate_up.shape
+        inter, top = two_inter // 2, choice.shape[1]
+        pairs = T * top
+        if x.dtype != w_gate_up.dtype or x.stride(1) != 1 or not w_gate_up.is_contiguous() or not w_down.is_contiguous():
+            raise KernelError("routed_experts: operands must share a dtype and be contiguous")
+        offsets = torch.empty(E + 1, dtype=torch.int32, device=self.device)
+        order = torch.empty(pairs, dtype=torch.int32, device=self.device)
+        self._check(self.lib.ttb_moe_align(self._p(choice), pairs, E, self._p(offsets), self._p(order), self._stream()),
+                    "moe_align")
+        hidden = torch.empty(pairs, inter, dtype=x.dtype, device=self.device)
+        code = _dtype_code(x.dtype)
+        self._check(self.lib.ttb_moe_group_gemm(
+            self._p(x), x.stride(0), self._p(w_gate_up), ctypes.c_longlong(two_inter * width), width, self._p(hidden), inter,
+            code, 1, self._p(offsets), self._p(order), pairs, E, top, inter, width, ctypes.c_float(limit),
+            ctypes.c_float(alpha), self._stream()), "moe_gate_up")
+        pair_out = torch.empty(pairs, width, dtype=torch.float32, device=self.device)
+        self._check(self.lib.ttb_moe_group_gemm(
+            self._p(hidden), inter, self._p(w_down), ctypes.c_longlong(width * inter), inter, self._p(pair_out), width,
+            code, 0, self._p(offsets), self._p(order), pairs, E, top, width, inter, ctypes.c_float(limit),
+            ctypes.c_float(alpha), self._stream()), "moe_down")
+        out = torch.empty(T, width, dtype=torch.float32, device=self.device)
+        if shared_out is not None and (shared_out.shape != (T, width) or not shared_out.is_contiguous()):
+            raise KernelError("routed_experts: the shared expert's output must be contiguous [T, width]")
+        self._check(self.lib.ttb_moe_combine(
+            self._p(pair_out), self._p(weight), top, self._p(shared_out),
+            _dtype_code(shared_out.dtype) if shared_out is not None else 0, self._p(shared_gate), self._p(out), T, width,
+            self._stream()), "moe_combine")
+        return out
 
     # ------------------------------------------------------------------ sampling
     def sample(self, logits, temperature=None, top_k=None, top_p=None, seeds=None, counters=None) -> torch.Tensor:
