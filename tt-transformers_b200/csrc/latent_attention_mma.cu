@@ -1,0 +1,322 @@
+// Attention over paged latents on the tensor cores (mma.sync m16n8k16, bfloat16 in, float32 sums and softmax).
+//
+// All heads of a token read the same cache rows [latent | extra], so a tile's 64 query rows are (token, head)
+// pairs: the heads of 64 / heads tokens, or, with more than 64 heads, a group of 64 heads of one token. A block
+// walks the keys of its segment in tiles of 64 that start at multiples of 64 from position 0 (the order of summation
+// for a query does not depend on how its request was cut into steps): S = Q K^T over latent + extra elements,
+// online softmax in float32 (base 2, the scale folded in), O += P C, where the values C are the latent part of
+// the very rows that served as keys, read from the same shared-memory tile with transposing loads. The rotated
+// query part is rotated by its token's position while the tile is loaded. A sink starts the running maximum and
+// sum of a row at (sink, 1): one more term of the denominator without a value. Output columns are handled in
+// chunks of LM_CHUNK per block; key tiles may be split over blocks (decode, few tiles), which then leave float32
+// partial sums with their maxima for latent_attention_merge.
+//
+// Rows of the cache beyond the last visible key are never read (zeros take their place), so pages that were never
+// written cannot reach a result. Tiles are derived on the device from the segment bounds: blockIdx.x counts
+// (segment, tile in segment) up to the longest segment, blocks past their segment's end return at once.
+#include "common.cuh"
+
+#define LM_ROWS 64
+#define LM_KEYS 64
+#define LM_THREADS 128
+#define LM_CHUNK 128
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+struct LatentMmaArgs {
+    const __nv_bfloat16* q_lat; long long ql_stride_t, ql_stride_h;
+    const __nv_bfloat16* q_rot; long long qr_stride_t, qr_stride_h;
+    __nv_bfloat16* out;
+    const int* cu_seqlens; const int* seg_pos0;
+    const __nv_bfloat16* rows; const int* block_table; int table_width, page_size, num_pages;
+    int heads, heads_per_group, tokens_per_tile, tiles_per_seg, chunks;
+    int latent, extra, rotary_dim;
+    float scale_log2; const float* sinks; const float* inv_freq;
+    int splits; float* partial_o; float* partial_ml; int* status;
+};
+
+__global__ void __launch_bounds__(LM_THREADS)
+latent_attention_mma_kernel(const LatentMmaArgs a) {
+    extern __shared__ __align__(16) unsigned char lm_smem[];
+    const int dk = a.latent + a.extra, ldq = dk + 8, vecs = dk / 8;
+    __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(lm_smem);      // [LM_ROWS][ldq]
+    __nv_bfloat16* Ks = Qs + LM_ROWS * ldq;                              // [LM_KEYS][ldq]
+    pdl_wait();
+    const int seg = blockIdx.x / a.tiles_per_seg, tile_in_seg = blockIdx.x % a.tiles_per_seg;
+    const int seg_begin = a.cu_seqlens[seg], seg_len = a.cu_seqlens[seg + 1] - seg_begin;
+    const int tok_off0 = tile_in_seg * a.tokens_per_tile;
+    if (tok_off0 >= seg_len) { pdl_launch_dependents(); return; }
+    const int ntok = min(a.tokens_per_tile, seg_len - tok_off0);
+    const int pos0 = a.seg_pos0[seg] + tok_off0;            // position of the tile's first token
+    const int hgroup = blockIdx.y / a.chunks, chunk = blockIdx.y % a.chunks;
+    const int h0 = hgroup * a.heads_per_group, nh = min(a.heads_per_group, a.heads - h0);
+    const int col0 = chunk * LM_CHUNK, ncols = min(LM_CHUNK, a.latent - col0);
+    const int valid_rows = ntok * nh;                        // row r: token r / nh of the tile, head h0 + r % nh
+    const int split = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t4 = lane & 3;
+    const int* table = a.block_table + (size_t)seg * a.table_width;
+
+    // ---- the query tile: latent part as it is, rotated part rotated by the token's position
+    const int lat_vecs = a.latent / 8;
+    for (int i = tid; i < LM_ROWS * lat_vecs; i += LM_THREADS) {
+        const int r = i / lat_vecs, c = (i % lat_vecs) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < valid_rows) {
+            const size_t tok = seg_begin + tok_off0 + r / nh;
+            v = *reinterpret_cast<const uint4*>(a.q_lat + tok * a.ql_stride_t + (size_t)(h0 + r % nh) * a.ql_stride_h + c);
+        }
+        *reinterpret_cast<uint4*>(Qs + r * ldq + c) = v;
+    }
+    if (a.extra > 0) {
+        const int half = a.rotary_dim / 2;
+        for (int i = tid; i < LM_ROWS * a.extra; i += LM_THREADS) {
+            const int r = i / a.extra, d = i % a.extra;
+            float v = 0.f;
+            if (r < valid_rows) {
+                const size_t tok = seg_begin + tok_off0 + r / nh;
+                const __nv_bfloat16* src = a.q_rot + tok * a.qr_stride_t + (size_t)(h0 + r % nh) * a.qr_stride_h;
+                v = __bfloat162float(src[d]);
+                if (d < a.rotary_dim) {
+                    const int f = d < half ? d : d - half;
+                    float sn, cs;
+                    sincosf((float)(pos0 + r / nh) * a.inv_freq[f], &sn, &cs);
+                    const float other = __bfloat162float(src[d < half ? d + half : d - half]);
+                    v = d < half ? v * cs - other * sn : v * cs + other * sn;
+                }
+            }
+            Qs[r * ldq + a.latent + d] = __float2bfloat16_rn(v);
+        }
+    }
+
+    // ---- which key tiles are this block's
+    const int last_key = pos0 + ntok - 1;
+    const int nk = last_key / LM_KEYS + 1;
+    const int per = (nk + a.splits - 1) / a.splits;
+    const int kt_begin = split * per, kt_end = min(nk, kt_begin + per);
+
+    const int r0 = warp * 16 + g, r1 = r0 + 8;
+    const int row_pos0 = r0 < valid_rows ? pos0 + r0 / nh : -1;      // -1: no key is visible, the row is idle
+    const int row_pos1 = r1 < valid_rows ? pos0 + r1 / nh : -1;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    if (a.sinks != nullptr && split == 0) {            // the sink: a term of the denominator without a value
+        const float log2e = 1.4426950408889634f;
+        if (r0 < valid_rows) { m0 = a.sinks[h0 + r0 % nh] * log2e; l0 = t4 == 0 ? 1.f : 0.f; }
+        if (r1 < valid_rows) { m1 = a.sinks[h0 + r1 % nh] * log2e; l1 = t4 == 0 ? 1.f : 0.f; }
+    }
+    float o[LM_CHUNK / 8][4];
+#pragma unroll
+    for (int j = 0; j < LM_CHUNK / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+
+    for (int kt = kt_begin; kt < kt_end; ++kt) {
+        __syncthreads();                                 // the query tile is written; the last key tile is read
+        for (int i = tid; i < LM_KEYS * vecs; i += LM_THREADS) {
+            const int r = i / vecs, c = (i % vecs) * 8;
+            const int key = kt * LM_KEYS + r;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (key <= last_key) {
+                const int page = table[key / a.page_size];
+                if ((unsigned)page < (unsigned)a.num_pages)
+                    v = *reinterpret_cast<const uint4*>(a.rows + ((size_t)page * a.page_size + key % a.page_size) * dk + c);
+                else if (c == 0) atomicExch(a.status, 0x2000000 + seg_begin + tok_off0);
+            }
+            *reinterpret_cast<uint4*>(Ks + r * ldq + c) = v;
+        }
+        __syncthreads();
+        float s[LM_KEYS / 8][4];
+#pragma unroll
+        for (int j = 0; j < LM_KEYS / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+        for (int k0 = 0; k0 < dk; k0 += 16) {
+            uint32_t qa[4];
+            ldsm_x4(qa, Qs + (warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ldq + k0 + (lane >> 4) * 8);
+#pragma unroll
+            for (int jp = 0; jp < LM_KEYS / 16; ++jp) {
+                uint32_t kb[4];
+                ldsm_x4(kb, Ks + (jp * 16 + (lane & 7) + (lane >> 4) * 8) * ldq + k0 + ((lane >> 3) & 1) * 8);
+                mma_bf16(s[2 * jp], qa, kb[0], kb[1]);
+                mma_bf16(s[2 * jp + 1], qa, kb[2], kb[3]);
+            }
+        }
+        // scale, mask, running maximum
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < LM_KEYS / 8; ++j) {
+            const int key = kt * LM_KEYS + 8 * j + 2 * t4;
+            s[j][0] = key <= row_pos0 ? s[j][0] * a.scale_log2 : -INFINITY;
+            s[j][1] = key + 1 <= row_pos0 ? s[j][1] * a.scale_log2 : -INFINITY;
+            s[j][2] = key <= row_pos1 ? s[j][2] * a.scale_log2 : -INFINITY;
+            s[j][3] = key + 1 <= row_pos1 ? s[j][3] * a.scale_log2 : -INFINITY;
+            mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+            mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+        const float base0 = n0 == -INFINITY ? 0.f : n0, base1 = n1 == -INFINITY ? 0.f : n1;
+        const float corr0 = exp2f(m0 - base0), corr1 = exp2f(m1 - base1);     // exp2(-inf) = 0
+        m0 = n0;
+        m1 = n1;
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < LM_KEYS / 8; ++j) {
+            s[j][0] = exp2f(s[j][0] - base0);
+            s[j][1] = exp2f(s[j][1] - base0);
+            s[j][2] = exp2f(s[j][2] - base1);
+            s[j][3] = exp2f(s[j][3] - base1);
+            sum0 += s[j][0] + s[j][1];
+            sum1 += s[j][2] + s[j][3];
+        }
+        l0 = l0 * corr0 + sum0;
+        l1 = l1 * corr1 + sum1;
+#pragma unroll
+        for (int j = 0; j < LM_CHUNK / 8; ++j) {
+            o[j][0] *= corr0; o[j][1] *= corr0; o[j][2] *= corr1; o[j][3] *= corr1;
+        }
+        // O += P C: the values are the latent part of the key rows
+#pragma unroll
+        for (int kk = 0; kk < LM_KEYS / 16; ++kk) {
+            uint32_t pa[4];
+            pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+            pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+            pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+            for (int np = 0; np < LM_CHUNK / 16; ++np) {
+                if (np * 16 < ncols) {
+                    uint32_t vb[4];
+                    ldsm_x4_trans(vb, Ks + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ldq + col0 + np * 16 + (lane >> 4) * 8);
+                    mma_bf16(o[2 * np], pa, vb[0], vb[1]);
+                    mma_bf16(o[2 * np + 1], pa, vb[2], vb[3]);
+                }
+            }
+        }
+    }
+    pdl_launch_dependents();
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+#pragma unroll
+    for (int half_row = 0; half_row < 2; ++half_row) {
+        const int r = half_row ? r1 : r0;
+        if (r >= valid_rows) continue;
+        const float m = half_row ? m1 : m0, l = half_row ? l1 : l0;
+        const size_t row = (size_t)(seg_begin + tok_off0 + r / nh) * a.heads + h0 + r % nh;
+        if (a.splits == 1) {
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            __nv_bfloat16* dst = a.out + row * a.latent + col0;
+#pragma unroll
+            for (int j = 0; j < LM_CHUNK / 8; ++j)
+                if (j * 8 < ncols)
+                    *reinterpret_cast<uint32_t*>(dst + j * 8 + 2 * t4) = pack_bf16(o[j][2 * half_row] * inv, o[j][2 * half_row + 1] * inv);
+        } else {
+            float* dst = a.partial_o + (row * a.splits + split) * a.latent + col0;
+#pragma unroll
+            for (int j = 0; j < LM_CHUNK / 8; ++j)
+                if (j * 8 < ncols)
+                    *reinterpret_cast<float2*>(dst + j * 8 + 2 * t4) = make_float2(o[j][2 * half_row], o[j][2 * half_row + 1]);
+            if (chunk == 0 && t4 == 0) {
+                a.partial_ml[(row * a.splits + split) * 2] = m;
+                a.partial_ml[(row * a.splits + split) * 2 + 1] = l;
+            }
+        }
+    }
+}
+
+// out[row, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s, splits in their order.
+__global__ void latent_attention_merge_kernel(const float* __restrict__ partial_o, const float* __restrict__ partial_ml,
+                                              __nv_bfloat16* __restrict__ out, int splits, int latent) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const size_t row = blockIdx.x;
+    const float* ml = partial_ml + row * splits * 2;
+    float M = -INFINITY;
+    for (int s = 0; s < splits; ++s) M = fmaxf(M, ml[2 * s]);
+    float denom = 0.f;
+    for (int s = 0; s < splits; ++s) denom += ml[2 * s] == -INFINITY ? 0.f : exp2f(ml[2 * s] - M) * ml[2 * s + 1];
+    const float inv = denom > 0.f ? 1.f / denom : 0.f;
+    for (int c = threadIdx.x; c < latent; c += blockDim.x) {
+        float acc = 0.f;
+        for (int s = 0; s < splits; ++s)
+            if (ml[2 * s] != -INFINITY) acc += exp2f(ml[2 * s] - M) * partial_o[(row * splits + s) * latent + c];
+        out[row * latent + c] = __float2bfloat16_rn(acc * inv);
+    }
+}
+
+TTB_EXPORT int ttb_latent_attention_mma_supports(int latent, int extra, int rotary_dim, int window) {
+    if (latent < 16 || (latent & 15) || (extra & 15) || extra < 0 || window > 0) return 0;
+    if (rotary_dim > extra || (rotary_dim & 1)) return 0;
+    const size_t smem = (size_t)(LM_ROWS + LM_KEYS) * (latent + extra + 8) * 2;
+    return smem <= 220 * 1024;
+}
+
+// Tokens whose heads share a tile, for the caller's split heuristics.
+TTB_EXPORT int ttb_latent_attention_mma_tokens_per_tile(int heads) {
+    const int hg = heads < LM_ROWS ? heads : LM_ROWS;
+    return LM_ROWS / hg > 0 ? LM_ROWS / hg : 1;
+}
+
+// q_lat [tokens, heads, latent] and q_rot [tokens, heads, extra] with element strides (token, head, 1), 16-byte
+// aligned rows; out [tokens, heads, latent] contiguous; rows [num_pages, page_size, latent + extra]. With
+// splits > 1: partial_o tokens * heads * splits * latent floats, partial_ml tokens * heads * splits * 2 floats.
+TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t, long long ql_stride_h, const void* q_rot,
+                                        long long qr_stride_t, long long qr_stride_h, void* out, const int* cu_seqlens,
+                                        const int* seg_pos0, const void* rows, const int* block_table, int table_width,
+                                        int page_size, int num_pages, int segments, int max_seg_len, int tokens, int heads,
+                                        int latent, int extra, float scale, const float* sinks, const float* inv_freq,
+                                        int rotary_dim, int splits, float* partial_o, float* partial_ml, int* status,
+                                        cudaStream_t stream) {
+    if (tokens == 0 || segments == 0) return TTB_OK;
+    if (!q_lat || !out || !cu_seqlens || !seg_pos0 || !rows || !block_table || !status) return TTB_ERR_ARGUMENT;
+    if (!ttb_latent_attention_mma_supports(latent, extra, rotary_dim, 0)) return TTB_ERR_UNSUPPORTED;
+    if (extra > 0 && (!q_rot || (rotary_dim > 0 && !inv_freq))) return TTB_ERR_ARGUMENT;
+    if ((ql_stride_t & 7) || (ql_stride_h & 7) || !aligned16(q_lat) || !aligned16(rows) || !aligned16(out)) return TTB_ERR_ARGUMENT;
+    if (splits < 1 || splits > 65535 || (splits > 1 && (!partial_o || !partial_ml))) return TTB_ERR_ARGUMENT;
+    LatentMmaArgs a;
+    a.q_lat = (const __nv_bfloat16*)q_lat; a.ql_stride_t = ql_stride_t; a.ql_stride_h = ql_stride_h;
+    a.q_rot = (const __nv_bfloat16*)q_rot; a.qr_stride_t = qr_stride_t; a.qr_stride_h = qr_stride_h;
+    a.out = (__nv_bfloat16*)out; a.cu_seqlens = cu_seqlens; a.seg_pos0 = seg_pos0;
+    a.rows = (const __nv_bfloat16*)rows; a.block_table = block_table; a.table_width = table_width;
+    a.page_size = page_size; a.num_pages = num_pages; a.heads = heads;
+    a.heads_per_group = heads < LM_ROWS ? heads : LM_ROWS;
+    a.tokens_per_tile = ttb_latent_attention_mma_tokens_per_tile(heads);
+    a.tiles_per_seg = (max_seg_len + a.tokens_per_tile - 1) / a.tokens_per_tile;
+    a.chunks = (latent + LM_CHUNK - 1) / LM_CHUNK;
+    a.latent = latent; a.extra = extra; a.rotary_dim = rotary_dim;
+    a.scale_log2 = scale * 1.4426950408889634f; a.sinks = sinks; a.inv_freq = inv_freq;
+    a.splits = splits; a.partial_o = partial_o; a.partial_ml = partial_ml; a.status = status;
+    const long long blocks_x = (long long)segments * a.tiles_per_seg;
+    const int groups = (heads + a.heads_per_group - 1) / a.heads_per_group;
+    if (blocks_x > 2147483647LL || groups * a.chunks > 65535) return TTB_ERR_UNSUPPORTED;
+    const size_t smem = (size_t)(LM_ROWS + LM_KEYS) * (latent + extra + 8) * 2;
+    static TtbOncePerDevice once;
+    if (once.pending()) {
+        cudaFuncSetAttribute(latent_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        once.mark();
+    }
+    ttb_launch(latent_attention_mma_kernel, dim3((unsigned)blocks_x, groups * a.chunks, splits), LM_THREADS, smem, stream, a);
+    int rc = ttb_launch_status();
+    if (rc != TTB_OK || splits == 1) return rc;
+    ttb_launch(latent_attention_merge_kernel, tokens * heads, 128, 0, stream, (const float*)partial_o,
+               (const float*)partial_ml, (__nv_bfloat16*)out, splits, latent);
+    return ttb_launch_status();
+}

@@ -95,7 +95,9 @@ class CudaKernels:
                      "ttb_gemm_skinny_tcgen05", "ttb_gemm_skinny_tcgen05_rows", "ttb_softcap", "ttb_sample_scratch_bytes",
                      "ttb_gemv_ring", "ttb_gemm_skinny_tcgen05_qkv_rope", "ttb_add_layernorm", "ttb_latent_prepare",
                      "ttb_latent_attention_generic", "ttb_gate_heads", "ttb_gemm_simt_batched", "ttb_route_top",
-                     "ttb_moe_align", "ttb_moe_group_gemm", "ttb_moe_combine", "ttb_glu_clamped"):
+                     "ttb_moe_align", "ttb_moe_group_gemm", "ttb_moe_combine", "ttb_glu_clamped",
+                     "ttb_latent_attention_mma", "ttb_latent_attention_mma_supports",
+                     "ttb_latent_attention_mma_tokens_per_tile"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -106,6 +108,8 @@ class CudaKernels:
         self.launches = 0     # how many of our kernels were launched (counted for reports)
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.use_mma_attention = True
+        # latent attention in bfloat16 on the tensor cores (False: the float32-arithmetic kernel everywhere)
+        self.use_mma_latent_attention = os.environ.get("TTB200_MMA_LATENT", "1") == "1"
         # prompt portions at head size 64: the TMA + tcgen05 attention kernel (False: the mma.sync one)
         self.use_tcgen05_attention = os.environ.get("TTB200_TCGEN05_ATTENTION", "1") == "1"
         # decode steps (up to 16 query rows per segment and KV head): the transposed-product kernel with TMA
@@ -650,6 +654,30 @@ class CudaKernels:
         if (q_rot is None) != (view.extra == 0) or (q_rot is not None and (q_rot.shape[2] != view.extra or q_rot.stride(2) != 1)):
             raise KernelError("latent_attention: the rotated query part does not fit the cache rows")
         out = torch.empty(T, H, R, dtype=q_latent.dtype, device=self.device)
+        if (self.use_mma_latent_attention and q_latent.dtype == torch.bfloat16 and view.rows.is_contiguous()
+                and q_latent.stride(0) % 8 == 0 and q_latent.stride(1) % 8 == 0 and q_latent.data_ptr() % 16 == 0
+                and self.lib.ttb_latent_attention_mma_supports(R, view.extra, int(rotary_dim), int(view.window or 0))):
+            # tensor cores; few blocks (decode): the keys are split over blocks and merged afterwards
+            per_tile = int(self.lib.ttb_latent_attention_mma_tokens_per_tile(H))
+            blocks = batch.num_segments * -(-batch.max_seg_len // per_tile) * -(-H // 64) * -(-R // 128)
+            splits = 1
+            if blocks < self.sm_count:
+                splits = max(1, min(-(-2 * self.sm_count // blocks), batch.max_context // 256, 64))
+            partial_o = partial_ml = None
+            if splits > 1:
+                partial_o = torch.empty(T * H * splits * R, dtype=torch.float32, device=self.device)
+                partial_ml = torch.empty(T * H * splits * 2, dtype=torch.float32, device=self.device)
+            self._check(self.lib.ttb_latent_attention_mma(
+                self._p(q_latent), ctypes.c_longlong(q_latent.stride(0)), ctypes.c_longlong(q_latent.stride(1)),
+                self._p(q_rot), ctypes.c_longlong(q_rot.stride(0) if q_rot is not None else 0),
+                ctypes.c_longlong(q_rot.stride(1) if q_rot is not None else 0), self._p(out), self._p(batch.cu_seqlens),
+                self._p(batch.seg_pos0), self._p(view.rows), self._p(view.block_table), view.block_table.shape[1],
+                view.page_size, view.rows.shape[0], batch.num_segments, batch.max_seg_len, T, H, R, view.extra,
+                ctypes.c_float(scale), self._p(sinks), self._p(inv_freq), int(rotary_dim), splits, self._p(partial_o),
+                self._p(partial_ml), self._p(self.status), self._stream()), "latent_attention_mma")
+            if splits > 1:
+                self.launches += 1
+            return out
         self._check(self.lib.ttb_latent_attention_generic(
             self._p(q_latent), ctypes.c_longlong(q_latent.stride(0)), ctypes.c_longlong(q_latent.stride(1)),
             self._p(q_rot), ctypes.c_longlong(q_rot.stride(0) if q_rot is not None else 0),
