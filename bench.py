@@ -50,6 +50,10 @@ def main(argv=None) -> int:
     parser.add_argument("--points", default="1,64", help="other decode batch sizes to report, comma separated")
     parser.add_argument("--skip-prefill", action="store_true", help="leave the prefill measurement out (for profiling decode)")
     parser.add_argument("--skip-e2e", action="store_true", help="leave the end-to-end measurement out (for profiling)")
+    parser.add_argument("--design", default=None,
+                        help="instead of the default workload: prefill and decode throughput of a named random model of "
+                             "another design (bozavik-a, bozavik-b) beside the closest dense model at equal size, with "
+                             "the design's own kernels against their rooflines")
     parser.add_argument("--fill", default="prefill", choices=("prefill", "synthetic"),
                         help="how the cache gets its context before decoding: through the engine's own prefill, "
                              "or filled with random numbers (faster; decode time does not depend on the values)")
@@ -62,6 +66,20 @@ def main(argv=None) -> int:
         print(f"bench.py: this engine runs on one GPU; --gpus {args.gpus} is not supported")
         return 2
     warmup = max(args.warmup, 3)
+
+    if args.design:
+        from tt_transformers_b200.cli import measure
+
+        context = min(args.context, 4096)
+        result = measure.run_design_comparison(args.design, batch=args.batch, context=context,
+                                               steps=min(args.steps, 32), warmup=warmup)
+        own = result["Bozavik"]
+        print(json.dumps({"metric": f"decode tokens/s, {args.design} sizes, batch {args.batch}", "value": own["decode_tokens_per_s"],
+                          "unit": "tokens/s", "n_gpus": 1, "steps": min(args.steps, 32), "warmup": warmup,
+                          "ms_per_step": own["decode_ms_per_step"], "higher_is_better": True, "dtype": "bf16",
+                          "data": "synthetic: random weights, uniform-random token ids",
+                          "config": {"model": args.design, "global_batch": args.batch, "seq_len": context}, "comparison": result}))
+        return 0
 
     from tt_transformers_b200.cli import measure
     from tt_transformers_b200.engine.llm import LLM

@@ -30,6 +30,44 @@ RANDOM_MODELS = {
 }
 
 
+def bozavik_config(width, layers, heads, dim, rot_dim, vdim, q_rank, kv_rank, experts, top, ff, shared_ff, vocab):
+    """Layers alternate between the two latent-attention mixers; every layer has the routed feed-forward."""
+    def mixer(second):
+        m = {"heads": heads, "dim": dim, "vdim": vdim, "q_rank": q_rank, "kv_rank": kv_rank,
+             "scale": (dim + (rot_dim if second else 0)) ** -0.5}
+        if second:
+            m.update(rot_dim=rot_dim, rot={"base": 500000.0, "dims": rot_dim})
+        return m
+
+    mlp = {"kind": "moe", "router": {"experts": experts, "top": top}, "expert": {"ff": ff, "limit": 7.0},
+           "shared": {"ff": shared_ff, "limit": 7.0}}
+    return {"architecture": "Bozavik", "vocab": vocab, "width": width, "residual_mult": 0.5, "norm": {"eps": 1e-6},
+            "embedding": {"scale": 1.0},
+            "layers": [{"type": "latent_attention_2" if i % 2 else "latent_attention", "mixer": mixer(i % 2 == 1),
+                        "mlp": mlp} for i in range(layers)]}
+
+
+def closest_llama(cfg: dict) -> dict:
+    """The dense decoder of this package that is closest to a Bozavik configuration: the same width, depth,
+    vocabulary and heads (head size = unrotated + rotated query elements), one KV head per four heads, and a
+    feed-forward as wide as the experts a token uses plus the shared one."""
+    layer = cfg["layers"][-1]
+    m, f = layer["mixer"], layer["mlp"]
+    heads, head_dim = m["heads"], m["dim"] + m.get("rot_dim", 0)
+    inter = f["router"]["top"] * f["expert"]["ff"] + (f.get("shared") or {}).get("ff", 0)
+    return {"architectures": ["LlamaForCausalLM"], "hidden_size": cfg["width"], "num_hidden_layers": len(cfg["layers"]),
+            "num_attention_heads": heads, "num_key_value_heads": max(1, heads // 4), "head_dim": head_dim,
+            "intermediate_size": inter, "vocab_size": cfg["vocab"], "rms_norm_eps": 1e-5,
+            "max_position_embeddings": 131072, "rope_theta": 500000.0, "tie_word_embeddings": False}
+
+
+RANDOM_MODELS.update({
+    "bozavik-tiny": bozavik_config(128, 2, 4, 16, 16, 16, 64, 64, 4, 2, 64, 64, 512),
+    "bozavik-a": bozavik_config(1024, 8, 16, 32, 32, 64, 384, 128, 16, 4, 512, 1024, 32768),
+    "bozavik-b": bozavik_config(2048, 8, 16, 64, 64, 128, 768, 256, 32, 4, 1024, 2048, 65536),
+})
+
+
 def load(hf_model, random_model, *, seed=0, **engine_options):
     """An LLM from a model folder, or from a named random model (weights drawn on the GPU)."""
     from ..config.engine import EngineConfig

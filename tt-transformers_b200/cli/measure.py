@@ -494,3 +494,184 @@ def run_token_match(cfg: dict, *, layers: Optional[int] = None, prompt_lengths=(
     return {"dtype": dtype, "layers": layers, "prompt_lengths": list(prompt_lengths), "plain_seconds": round(plain_s, 2),
             "modes": modes, "max_relative_error": max(m["max_relative_error"] for m in modes.values()),
             "argmax_agreement": min(m["argmax_agreement"] for m in modes.values())}
+
+
+# ---------------------------------------------------------------------------- a design beside its closest dense model
+class KernelTimer:
+    """CUDA events around the calls of named entries of an engine's kernel table (outermost calls only), for
+    steps that run eagerly. The device is kept busy ahead of a step (`hold`), so that the host's launch gaps
+    do not lie between a pair of events."""
+
+    def __init__(self, kernels, names):
+        self.kernels, self.names, self.records, self.depth = kernels, names, [], 0
+        self._originals = {}
+
+    def __enter__(self):
+        for name in self.names:
+            original = getattr(self.kernels, name)
+            self._originals[name] = original
+
+            def wrapped(*args, _original=original, _name=name, **kwargs):
+                if self.depth:
+                    return _original(*args, **kwargs)
+                self.depth += 1
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                try:
+                    return _original(*args, **kwargs)
+                finally:
+                    end.record()
+                    self.records.append((_name, start, end))
+                    self.depth -= 1
+
+            setattr(self.kernels, name, wrapped)
+        return self
+
+    def __exit__(self, *exc):
+        for name in self.names:
+            delattr(self.kernels, name)               # the instance attribute goes, the class's method shows again
+        return False
+
+    @staticmethod
+    def hold(ms: float = 5.0):
+        torch.cuda._sleep(int(ms * 1.8e6))            # the device spins while the host queues the step
+
+    def totals(self) -> Dict[str, float]:
+        torch.cuda.synchronize()
+        out: Dict[str, float] = {}
+        for name, start, end in self.records:
+            out[name] = out.get(name, 0.0) + start.elapsed_time(end) * 1e3
+        self.records = []
+        return out                                     # microseconds per name
+
+
+_TIMED = {"Bozavik": ["add_layernorm", "latent_prepare", "heads_linear", "latent_attention", "gate_heads", "route_top",
+                      "routed_experts", "linear_glu_clamped", "linear"],
+          "Llama": ["add_rmsnorm", "rope_kv_write", "fused_qkv_rope", "paged_attention", "linear_swiglu", "linear"]}
+
+
+def _kernel_work(cfg: dict, tokens: int, contexts: List[int], new_per_request: int) -> Dict[str, dict]:
+    """Algorithmic FLOPs and bytes per step of the kernels that are the design's own, per layer summed over the
+    layers: {kernel name: {"flops": .., "bytes": ..}}. contexts: tokens each request holds after the step."""
+    work: Dict[str, dict] = {}
+
+    def add(name, flops, nbytes):
+        w = work.setdefault(name, {"flops": 0.0, "bytes": 0.0})
+        w["flops"] += flops
+        w["bytes"] += nbytes
+
+    if cfg.get("architecture") == "Bozavik":
+        width = cfg["width"]
+        for layer in cfg["layers"]:
+            m, f = layer["mixer"], layer["mlp"]
+            dk = m["kv_rank"] + m.get("rot_dim", 0)
+            pairs = sum(n * new_per_request - new_per_request * (new_per_request - 1) / 2 for n in contexts)   # visible (query, key) pairs
+            add("latent_attention", 2 * m["heads"] * pairs * (dk + m["kv_rank"]),
+                2 * (sum(contexts) * dk + 2 * tokens * m["heads"] * m["kv_rank"]))
+            add("add_layernorm", 0, 2 * tokens * width * (4 + 4 + 2 + 2))
+            add("latent_prepare", 0, tokens * (4 * (m["q_rank"] + dk) + 2 * (m["q_rank"] + dk)))
+            if f:
+                top, ff, experts = f["router"]["top"], f["expert"]["ff"], f["router"]["experts"]
+                used = min(experts, tokens * top)
+                add("routed_experts", 2 * tokens * top * 3 * ff * width, 2 * used * 3 * ff * width + tokens * width * (2 + 4))
+    else:
+        width, heads, kv, hd = cfg["hidden_size"], cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
+        for _ in range(cfg["num_hidden_layers"]):
+            pairs = sum(n * new_per_request - new_per_request * (new_per_request - 1) / 2 for n in contexts)
+            add("paged_attention", 2 * heads * pairs * 2 * hd, 2 * (sum(contexts) * 2 * kv * hd + 2 * tokens * heads * hd))
+            add("add_rmsnorm", 0, 2 * tokens * width * (4 + 4 + 2 + 2) / 2 * 1.0)
+            add("rope_kv_write", 0, tokens * (heads + 2 * kv) * hd * 2 * 2)
+            inter = cfg["intermediate_size"]
+            add("linear_swiglu", 2 * tokens * 2 * inter * width, 2 * 2 * inter * width + tokens * (width + inter) * 2)
+    return work
+
+
+def _step_kernel_times(engine, family: str, entries_fn, reps: int = 3) -> Dict[str, float]:
+    """Microseconds per step and kernel name, eager steps, the best of `reps`."""
+    best: Dict[str, float] = {}
+    with KernelTimer(engine.kernels, _TIMED[family]) as timer:
+        for _ in range(reps + 1):
+            entries, finish = entries_fn()
+            KernelTimer.hold()
+            engine.step(entries)
+            got = timer.totals()
+            for rid in finish:
+                engine.finish(rid)
+            for name, us in got.items():
+                best[name] = min(best.get(name, float("inf")), us)
+    return best
+
+
+def run_design_comparison(name: str = "bozavik-a", *, prefill_tokens: int = PREFILL_TOKENS, batch: int = 8,
+                          context: int = 4096, steps: int = 32, warmup: int = 4, device: str = "cuda:0") -> dict:
+    """Prefill and decode throughput of a named Bozavik model (random weights) and of the dense decoder closest to
+    it at equal size, and, kernel by kernel, how far the design's own kernels are from their rooflines beside the
+    like kernels of the dense model (eager steps, CUDA events around each kernel-table call)."""
+    from ..engine.step import StepEntry
+    from .common import closest_llama
+
+    pk = peaks()
+    out = {"model": name, "peaks": pk["source"], "prefill_tokens": prefill_tokens, "decode": {"batch": batch, "context": context}}
+    configs = {"Bozavik": dict(RANDOM_MODELS[name])}
+    configs["Llama"] = closest_llama(configs["Bozavik"])
+    for family, cfg in configs.items():
+        vocab = cfg.get("vocab", cfg.get("vocab_size"))
+        prompts = Prompts(vocab)
+        res = {}
+        engine = make_engine(cfg, max_batch=batch, context=context, device=device)
+        ids = prompts(prefill_tokens)
+
+        def once():
+            engine.step([StepEntry("p", ids, [prefill_tokens - 1])])
+            engine.finish("p")
+
+        for _ in range(3):
+            once()
+        ms = statistics.median(timed(once, 3) for _ in range(3))
+        res["prefill_ms"] = round(ms, 3)
+        res["prefill_tokens_per_s"] = round(prefill_tokens / ms * 1e3, 1)
+        start = context - steps - warmup - 1
+        rids = fill_requests(engine, cfg, batch, start, prompts, "synthetic")
+        tokens = engine.decode_steps(rids, [1] * batch, warmup)[-1]
+        before = engine.kernels.launches
+        ms = timed(lambda: engine.decode_steps(rids, tokens, steps), 1) / steps
+        res["decode_ms_per_step"] = round(ms, 4)
+        res["decode_tokens_per_s"] = round(batch / ms * 1e3, 1)
+        res["decode_launches_per_step"] = (engine.kernels.launches - before) // steps
+        for rid in rids:
+            engine.finish(rid)
+        engine.close()
+        # kernel by kernel, eagerly
+        engine = make_engine(cfg, max_batch=batch, context=context, device=device, cuda_graph=False)
+        table = {}
+        times = _step_kernel_times(engine, family, lambda: ([StepEntry("p", ids, [prefill_tokens - 1])], ["p"]))
+        work = _kernel_work(cfg, prefill_tokens, [prefill_tokens], prefill_tokens)
+        table["prefill"] = _roofline_rows(times, work, pk)
+        rids = fill_requests(engine, cfg, batch, start, prompts, "synthetic")
+        times = _step_kernel_times(engine, family, lambda: ([StepEntry(r, [1], [0]) for r in rids], []))
+        held = [engine.cache.length(r) for r in rids]
+        work = _kernel_work(cfg, batch, held, 1)
+        table["decode"] = _roofline_rows(times, work, pk)
+        for rid in rids:
+            engine.finish(rid)
+        engine.close()
+        res["kernels"] = table
+        out[family] = res
+        del engine
+        torch.cuda.empty_cache()
+    return out
+
+
+def _roofline_rows(times: Dict[str, float], work: Dict[str, dict], pk: dict) -> Dict[str, dict]:
+    rows = {}
+    for name, us in sorted(times.items()):
+        row = {"us": round(us, 1)}
+        w = work.get(name)
+        if w and us > 0:
+            t_flops = w["flops"] / (pk["bf16_tflops"] * 1e12) * 1e6
+            t_bytes = w["bytes"] / (pk["hbm_gbs"] * 1e9) * 1e6
+            row["roofline_us"] = round(max(t_flops, t_bytes), 2)
+            row["bound"] = "tensor" if t_flops > t_bytes else "hbm"
+            row["frac"] = round(max(t_flops, t_bytes) / us, 4)
+        rows[name] = row
+    return rows

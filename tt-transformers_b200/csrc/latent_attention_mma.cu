@@ -41,16 +41,25 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// 16 bytes global -> shared without passing registers; `bytes` 0 writes zeros instead (the source is not read)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int bytes) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 struct LatentMmaArgs {
     const __nv_bfloat16* q_lat; long long ql_stride_t, ql_stride_h;
     const __nv_bfloat16* q_rot; long long qr_stride_t, qr_stride_h;
     __nv_bfloat16* out;
     const int* cu_seqlens; const int* seg_pos0;
     const __nv_bfloat16* rows; const int* block_table; int table_width, page_size, num_pages;
-    int heads, heads_per_group, tokens_per_tile, tiles_per_seg, chunks;
+    int heads, heads_per_group, tokens_per_tile, tiles_per_seg, chunks, segments;
     int latent, extra, rotary_dim;
     float scale_log2; const float* sinks; const float* inv_freq;
     int splits; float* partial_o; float* partial_ml; int* status;
+    int stages;      // key tiles in shared memory at a time: 2 (the next one is fetched under the products) or 1
 };
 
 __global__ void __launch_bounds__(LM_THREADS)
@@ -60,7 +69,8 @@ latent_attention_mma_kernel(const LatentMmaArgs a) {
     __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(lm_smem);      // [LM_ROWS][ldq]
     __nv_bfloat16* Ks = Qs + LM_ROWS * ldq;                              // [LM_KEYS][ldq]
     pdl_wait();
-    const int seg = blockIdx.x / a.tiles_per_seg, tile_in_seg = blockIdx.x % a.tiles_per_seg;
+    // the tiles at the end of a segment see the most keys: they start first
+    const int seg = blockIdx.x % a.segments, tile_in_seg = a.tiles_per_seg - 1 - blockIdx.x / a.segments;
     const int seg_begin = a.cu_seqlens[seg], seg_len = a.cu_seqlens[seg + 1] - seg_begin;
     const int tok_off0 = tile_in_seg * a.tokens_per_tile;
     if (tok_off0 >= seg_len) { pdl_launch_dependents(); return; }
@@ -125,21 +135,37 @@ latent_attention_mma_kernel(const LatentMmaArgs a) {
 #pragma unroll
     for (int j = 0; j < LM_CHUNK / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 
-    for (int kt = kt_begin; kt < kt_end; ++kt) {
-        __syncthreads();                                 // the query tile is written; the last key tile is read
-        for (int i = tid; i < LM_KEYS * vecs; i += LM_THREADS) {
-            const int r = i / vecs, c = (i % vecs) * 8;
+    // one key tile into shared memory: a warp per row, 16-byte copies that bypass the registers; rows past the last
+    // visible key (and rows of pages outside the pool) become zeros
+    auto fetch = [&](int kt, __nv_bfloat16* dst) {
+        for (int r = warp; r < LM_KEYS; r += LM_THREADS / 32) {
             const int key = kt * LM_KEYS + r;
-            uint4 v = make_uint4(0, 0, 0, 0);
+            const __nv_bfloat16* src = a.rows;
+            int bytes = 0;
             if (key <= last_key) {
                 const int page = table[key / a.page_size];
-                if ((unsigned)page < (unsigned)a.num_pages)
-                    v = *reinterpret_cast<const uint4*>(a.rows + ((size_t)page * a.page_size + key % a.page_size) * dk + c);
-                else if (c == 0) atomicExch(a.status, 0x2000000 + seg_begin + tok_off0);
+                if ((unsigned)page < (unsigned)a.num_pages) {
+                    src = a.rows + ((size_t)page * a.page_size + key % a.page_size) * dk;
+                    bytes = 16;
+                } else if (lane == 0) {
+                    atomicExch(a.status, 0x2000000 + seg_begin + tok_off0);
+                }
             }
-            *reinterpret_cast<uint4*>(Ks + r * ldq + c) = v;
+            for (int c = lane; c < vecs; c += 32) cp_async16(dst + r * ldq + c * 8, bytes ? src + c * 8 : src, bytes);
         }
-        __syncthreads();
+        cp_async_commit();
+    };
+    const int second = a.stages == 2 ? LM_KEYS * ldq : 0;      // offset of the second key buffer (none: the same one)
+    if (kt_begin < kt_end) fetch(kt_begin, Ks);
+    for (int kt = kt_begin; kt < kt_end; ++kt) {
+        const __nv_bfloat16* Kt = Ks + ((kt - kt_begin) & 1) * second;
+        if (a.stages == 2 && kt + 1 < kt_end) {
+            fetch(kt + 1, Ks + ((kt + 1 - kt_begin) & 1) * second);     // lands while this tile is multiplied
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();                                     // the tile (and, first, the query tile) is in place
         float s[LM_KEYS / 8][4];
 #pragma unroll
         for (int j = 0; j < LM_KEYS / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
@@ -149,7 +175,7 @@ latent_attention_mma_kernel(const LatentMmaArgs a) {
 #pragma unroll
             for (int jp = 0; jp < LM_KEYS / 16; ++jp) {
                 uint32_t kb[4];
-                ldsm_x4(kb, Ks + (jp * 16 + (lane & 7) + (lane >> 4) * 8) * ldq + k0 + ((lane >> 3) & 1) * 8);
+                ldsm_x4(kb, Kt + (jp * 16 + (lane & 7) + (lane >> 4) * 8) * ldq + k0 + ((lane >> 3) & 1) * 8);
                 mma_bf16(s[2 * jp], qa, kb[0], kb[1]);
                 mma_bf16(s[2 * jp + 1], qa, kb[2], kb[3]);
             }
@@ -203,12 +229,14 @@ latent_attention_mma_kernel(const LatentMmaArgs a) {
             for (int np = 0; np < LM_CHUNK / 16; ++np) {
                 if (np * 16 < ncols) {
                     uint32_t vb[4];
-                    ldsm_x4_trans(vb, Ks + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ldq + col0 + np * 16 + (lane >> 4) * 8);
+                    ldsm_x4_trans(vb, Kt + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ldq + col0 + np * 16 + (lane >> 4) * 8);
                     mma_bf16(o[2 * np], pa, vb[0], vb[1]);
                     mma_bf16(o[2 * np + 1], pa, vb[2], vb[3]);
                 }
             }
         }
+        __syncthreads();                                     // all warps are done with this tile: it may be overwritten
+        if (a.stages == 1 && kt + 1 < kt_end) fetch(kt + 1, Ks);
     }
     pdl_launch_dependents();
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
@@ -301,13 +329,16 @@ TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t
     a.tokens_per_tile = ttb_latent_attention_mma_tokens_per_tile(heads);
     a.tiles_per_seg = (max_seg_len + a.tokens_per_tile - 1) / a.tokens_per_tile;
     a.chunks = (latent + LM_CHUNK - 1) / LM_CHUNK;
+    a.segments = segments;
     a.latent = latent; a.extra = extra; a.rotary_dim = rotary_dim;
     a.scale_log2 = scale * 1.4426950408889634f; a.sinks = sinks; a.inv_freq = inv_freq;
     a.splits = splits; a.partial_o = partial_o; a.partial_ml = partial_ml; a.status = status;
     const long long blocks_x = (long long)segments * a.tiles_per_seg;
     const int groups = (heads + a.heads_per_group - 1) / a.heads_per_group;
     if (blocks_x > 2147483647LL || groups * a.chunks > 65535) return TTB_ERR_UNSUPPORTED;
-    const size_t smem = (size_t)(LM_ROWS + LM_KEYS) * (latent + extra + 8) * 2;
+    const size_t tile_bytes = (size_t)LM_KEYS * (latent + extra + 8) * 2;
+    a.stages = 3 * tile_bytes <= 96 * 1024 ? 2 : 1;         // two key tiles only while several blocks still fit an SM
+    const size_t smem = (size_t)(1 + a.stages) * tile_bytes;
     static TtbOncePerDevice once;
     if (once.pending()) {
         cudaFuncSetAttribute(latent_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);

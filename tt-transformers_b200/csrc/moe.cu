@@ -24,10 +24,12 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
     extern __shared__ float rt_smem[];
     float* h = rt_smem;                   // [width]
     float* z = rt_smem + width;           // [experts + 1]
+    int* taken = reinterpret_cast<int*>(z + experts + 1);    // [experts]
     pdl_wait();
     pdl_launch_dependents();
     const int t = blockIdx.x;
     for (int c = threadIdx.x; c < width; c += RT_THREADS) h[c] = to_float(x[(size_t)t * ldx + c]);
+    for (int e = threadIdx.x; e < experts; e += RT_THREADS) taken[e] = 0;
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int e = warp; e < experts + (shared ? 1 : 0); e += RT_THREADS / 32) {
@@ -38,27 +40,39 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
         if (lane == 0) z[e] = s;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float best_first = 0.f, denom = 0.f;
+    // one warp picks: in round j every lane looks at its share of the experts that are still free, the lanes
+    // agree on the largest logit and, among equals, on the lowest index
+    if (warp == 0) {
+        float best_first = 0.f, denom = 0.f, mine = 0.f;
         for (int j = 0; j < top; ++j) {
-            int best = -1;
             float best_z = -INFINITY;
-            for (int e = 0; e < experts; ++e) {
-                const float v = z[e];
-                if (best < 0 || v > best_z) {
-                    bool taken = false;
-                    for (int i = 0; i < j; ++i) taken |= choice[(size_t)t * top + i] == e;
-                    if (!taken) { best = e; best_z = v; }
-                }
+            int best = 0x7fffffff;
+            for (int e = lane; e < experts; e += 32) {
+                const float v = taken[e] ? -INFINITY : z[e];
+                if (!taken[e] && (best == 0x7fffffff || v > best_z)) { best = e; best_z = v; }
             }
-            choice[(size_t)t * top + j] = best;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float oz = __shfl_xor_sync(0xffffffffu, best_z, o);
+                const int oe = __shfl_xor_sync(0xffffffffu, best, o);
+                if (oe != 0x7fffffff && (best == 0x7fffffff || oz > best_z || (oz == best_z && oe < best))) { best = oe; best_z = oz; }
+            }
+            if (lane == 0) taken[best] = 1;
+            __syncwarp();
             if (j == 0) best_first = best_z;
             const float p = expf(best_z - best_first);
-            weight[(size_t)t * top + j] = p;
             denom += p;
+            if (lane == j % 32) mine = p;                  // lane j keeps choice j's weight (top <= 32 per pass)
+            if (lane == 0) choice[(size_t)t * top + j] = best;
+            if ((j % 32 == 31 || j == top - 1)) {
+                // weights of this pass are normalised after the last round; park them unnormalised
+                const int base = j - j % 32;
+                if (base + lane <= j) weight[(size_t)t * top + base + lane] = mine;
+            }
         }
-        for (int j = 0; j < top; ++j) weight[(size_t)t * top + j] /= denom;
-        if (shared) shared_gate[t] = 1.f / (1.f + expf(-z[experts]));
+        __syncwarp();
+        for (int j = lane; j < top; j += 32) weight[(size_t)t * top + j] /= denom;
+        if (shared && lane == 0) shared_gate[t] = 1.f / (1.f + expf(-z[experts]));
     }
 }
 
@@ -67,7 +81,7 @@ TTB_EXPORT int ttb_route_top(const void* x, int dtype, int ldx, const float* w_r
     if (tokens == 0) return TTB_OK;
     if (!x || !w_router || !choice || !weight || (shared && !shared_gate)) return TTB_ERR_ARGUMENT;
     if (experts < 1 || experts > RT_MAX_EXPERTS || top < 1 || top > experts) return TTB_ERR_UNSUPPORTED;
-    const size_t smem = (size_t)(width + experts + 1) * sizeof(float);
+    const size_t smem = (size_t)(width + 2 * experts + 1) * sizeof(float);
     if (smem > 48 * 1024) return TTB_ERR_UNSUPPORTED;
     if (dtype == TTB_DTYPE_BF16)
         ttb_launch(route_top_kernel<__nv_bfloat16>, tokens, RT_THREADS, smem, stream, (const __nv_bfloat16*)x, ldx, w_router,
@@ -141,14 +155,15 @@ __device__ __forceinline__ float glu_clamped(float g, float u, float limit, floa
 }
 
 // Tile blockIdx.y of the pairs: walks the experts' groups in tiles of MG_BM rows. Returns false past the last tile.
-__device__ __forceinline__ bool mg_find_tile(const int* offsets, int experts, int tile, int& expert, int& row0, int& row_end) {
+__device__ __forceinline__ bool mg_find_tile(const int* offsets, int experts, int tile, int& expert, int& row0, int& row_end,
+                                             int bm = MG_BM) {
     int seen = 0;
     for (int e = 0; e < experts; ++e) {
         const int begin = offsets[e], end = offsets[e + 1];
-        const int tiles = (end - begin + MG_BM - 1) / MG_BM;
+        const int tiles = (end - begin + bm - 1) / bm;
         if (tile < seen + tiles) {
             expert = e;
-            row0 = begin + (tile - seen) * MG_BM;
+            row0 = begin + (tile - seen) * bm;
             row_end = end;
             return true;
         }
@@ -235,6 +250,134 @@ moe_group_gemm_kernel(const TA* __restrict__ A, int lda, const TA* __restrict__ 
     }
 }
 
+
+// ---------------------------------------------------------------- the same products on the tensor cores (bfloat16)
+// mma.sync m16n8k16, float32 accumulation: tiles of 64 pairs x 64 columns (FIRST: 64 gate and their 64 up rows
+// of W_e), K in steps of 64 through shared memory; four warps of 16 rows each.
+#define MM_BM 128
+#define MM_BN 64
+#define MM_BK 64
+#define MM_LD (MM_BK + 8)
+#define MM_THREADS 256
+#define MM_STAGE_ELEMS(first) ((MM_BM + ((first) ? 2 : 1) * MM_BN) * MM_LD)
+
+__device__ __forceinline__ void mm_ldsm_x4(uint32_t (&r)[4], const void* p) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void mm_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// 16 bytes global -> shared past the registers; `bytes` 0 writes zeros and reads nothing
+__device__ __forceinline__ void mm_cp16(void* dst, const void* src, int bytes) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+
+// Tiles of 128 pairs x 64 columns (FIRST: 64 gate rows of W_e and their 64 up rows), eight warps of 16 rows, K in
+// steps of 64 through two shared-memory stages: the next step's operands arrive (cp.async) under this step's products.
+template <bool FIRST>
+__global__ void __launch_bounds__(MM_THREADS)
+moe_group_gemm_mma_kernel(const __nv_bfloat16* __restrict__ A, int lda, const __nv_bfloat16* __restrict__ W,
+                          long long w_expert_stride, int ldw, void* __restrict__ C, int ldc,
+                          const int* __restrict__ offsets, const int* __restrict__ sorted, int experts, int top, int N,
+                          int K, float limit, float alpha) {
+    extern __shared__ __align__(16) unsigned char mm_smem[];
+    __nv_bfloat16* stage0 = reinterpret_cast<__nv_bfloat16*>(mm_smem);
+    __shared__ int src_row[MM_BM];
+    pdl_wait();
+    pdl_launch_dependents();
+    int expert, row0, row_end;
+    if (!mg_find_tile(offsets, experts, blockIdx.y, expert, row0, row_end, MM_BM)) return;
+    const int n0 = blockIdx.x * MM_BN;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t4 = lane & 3;
+    if (tid < MM_BM) {
+        const int r = row0 + tid;
+        src_row[tid] = r < row_end ? (FIRST ? sorted[r] / top : r) : -1;
+    }
+    __syncthreads();
+    const __nv_bfloat16* We = W + (size_t)expert * w_expert_stride;
+    auto fetch = [&](int k0, __nv_bfloat16* st) {
+        __nv_bfloat16* As = st;
+        __nv_bfloat16* Ws = st + MM_BM * MM_LD;
+        __nv_bfloat16* Us = Ws + MM_BN * MM_LD;
+        for (int i = tid; i < MM_BM * (MM_BK / 8); i += MM_THREADS) {
+            const int r = i / (MM_BK / 8), c = (i % (MM_BK / 8)) * 8;
+            const int src = src_row[r];
+            const bool in = src >= 0 && k0 + c < K;
+            mm_cp16(As + r * MM_LD + c, in ? A + (size_t)src * lda + k0 + c : A, in ? 16 : 0);
+        }
+        for (int i = tid; i < MM_BN * (MM_BK / 8); i += MM_THREADS) {
+            const int n = i / (MM_BK / 8), c = (i % (MM_BK / 8)) * 8;
+            const bool in = n0 + n < N && k0 + c < K;
+            mm_cp16(Ws + n * MM_LD + c, in ? We + (size_t)(n0 + n) * ldw + k0 + c : We, in ? 16 : 0);
+            if (FIRST) mm_cp16(Us + n * MM_LD + c, in ? We + (size_t)(N + n0 + n) * ldw + k0 + c : We, in ? 16 : 0);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    float acc[MM_BN / 8][4], acc_u[FIRST ? MM_BN / 8 : 1][4];
+#pragma unroll
+    for (int j = 0; j < MM_BN / 8; ++j) {
+        acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        if (FIRST) acc_u[j][0] = acc_u[j][1] = acc_u[j][2] = acc_u[j][3] = 0.f;
+    }
+    const int steps = (K + MM_BK - 1) / MM_BK;
+    fetch(0, stage0);
+    for (int step = 0; step < steps; ++step) {
+        const __nv_bfloat16* As = stage0 + (step & 1) * MM_STAGE_ELEMS(FIRST);
+        const __nv_bfloat16* Ws = As + MM_BM * MM_LD;
+        const __nv_bfloat16* Us = Ws + MM_BN * MM_LD;
+        if (step + 1 < steps) {
+            fetch((step + 1) * MM_BK, stage0 + ((step + 1) & 1) * MM_STAGE_ELEMS(FIRST));
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < MM_BK; kk += 16) {
+            uint32_t a[4];
+            mm_ldsm_x4(a, As + (warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * MM_LD + kk + (lane >> 4) * 8);
+#pragma unroll
+            for (int jp = 0; jp < MM_BN / 16; ++jp) {
+                uint32_t b[4];
+                mm_ldsm_x4(b, Ws + (jp * 16 + (lane & 7) + (lane >> 4) * 8) * MM_LD + kk + ((lane >> 3) & 1) * 8);
+                mm_mma(acc[2 * jp], a, b[0], b[1]);
+                mm_mma(acc[2 * jp + 1], a, b[2], b[3]);
+                if (FIRST) {
+                    mm_ldsm_x4(b, Us + (jp * 16 + (lane & 7) + (lane >> 4) * 8) * MM_LD + kk + ((lane >> 3) & 1) * 8);
+                    mm_mma(acc_u[2 * jp], a, b[0], b[1]);
+                    mm_mma(acc_u[2 * jp + 1], a, b[2], b[3]);
+                }
+            }
+        }
+        __syncthreads();              // this stage is read: the step after next may overwrite it
+    }
+#pragma unroll
+    for (int half_row = 0; half_row < 2; ++half_row) {
+        const int r = row0 + warp * 16 + g + 8 * half_row;
+        if (r >= row_end) continue;
+        const size_t dst = FIRST ? (size_t)r : (size_t)sorted[r];
+#pragma unroll
+        for (int j = 0; j < MM_BN / 8; ++j) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int n = n0 + 8 * j + 2 * t4 + e;
+                if (n >= N) continue;
+                const float v = acc[j][2 * half_row + e];
+                if (FIRST)
+                    reinterpret_cast<__nv_bfloat16*>(C)[dst * ldc + n] =
+                        __float2bfloat16_rn(glu_clamped(v, acc_u[j][2 * half_row + e], limit, alpha));
+                else
+                    reinterpret_cast<float*>(C)[dst * ldc + n] = v;
+            }
+        }
+    }
+}
+
 // first != 0: A = tokens [*, K], W = [experts, 2 N, K] (gate rows, then up rows), C = hidden [pairs, N] in the
 // grouped order, type of A. first == 0: A = hidden [pairs, K], W = [experts, N, K], C = float32 [pairs, N] by pair.
 TTB_EXPORT int ttb_moe_group_gemm(const void* A, int lda, const void* W, long long w_expert_stride, int ldw, void* C, int ldc,
@@ -242,6 +385,26 @@ TTB_EXPORT int ttb_moe_group_gemm(const void* A, int lda, const void* W, long lo
                                   int top, int N, int K, float limit, float alpha, cudaStream_t stream) {
     if (pairs == 0 || N == 0) return TTB_OK;
     if (!A || !W || !C || !offsets || !sorted || K < 1) return TTB_ERR_ARGUMENT;
+    if (dtype == TTB_DTYPE_BF16 && (K & 7) == 0 && (lda & 7) == 0 && (ldw & 7) == 0 && (w_expert_stride & 7) == 0 &&
+        aligned16(A) && aligned16(W)) {
+        dim3 tc_grid((N + MM_BN - 1) / MM_BN, (pairs + MM_BM - 1) / MM_BM + experts);
+        if (tc_grid.y > 65535) return TTB_ERR_UNSUPPORTED;
+        static TtbOncePerDevice once;
+        if (once.pending()) {
+            cudaFuncSetAttribute(moe_group_gemm_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 2 * MM_STAGE_ELEMS(true) * 2);
+            cudaFuncSetAttribute(moe_group_gemm_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 2 * MM_STAGE_ELEMS(false) * 2);
+            once.mark();
+        }
+        if (first)
+            ttb_launch(moe_group_gemm_mma_kernel<true>, tc_grid, MM_THREADS, 2 * MM_STAGE_ELEMS(true) * 2, stream, (const __nv_bfloat16*)A, lda,
+                       (const __nv_bfloat16*)W, w_expert_stride, ldw, C, ldc, offsets, sorted, experts, top, N, K, limit, alpha);
+        else
+            ttb_launch(moe_group_gemm_mma_kernel<false>, tc_grid, MM_THREADS, 2 * MM_STAGE_ELEMS(false) * 2, stream, (const __nv_bfloat16*)A, lda,
+                       (const __nv_bfloat16*)W, w_expert_stride, ldw, C, ldc, offsets, sorted, experts, top, N, K, limit, alpha);
+        return ttb_launch_status();
+    }
     dim3 grid((N + MG_BN - 1) / MG_BN, (pairs + MG_BM - 1) / MG_BM + experts);
     if (grid.y > 65535) return TTB_ERR_UNSUPPORTED;
 #define MG_LAUNCH(TA, TC, FIRST)                                                                                     \
@@ -255,6 +418,113 @@ TTB_EXPORT int ttb_moe_group_gemm(const void* A, int lda, const void* W, long lo
         return TTB_ERR_UNSUPPORTED;
     }
 #undef MG_LAUNCH
+    return ttb_launch_status();
+}
+
+
+// ---------------------------------------------------------------- a handful of tokens: the experts as matrix-vector products
+// Decode steps hold few (token, choice) pairs, most of them with an expert to themselves: every pair streams its
+// expert's rows straight from memory, a warp per output row, no grouping. moe_gemv_first: hidden[p, :] =
+// activation(W_gate,e x, W_up,e x) for pair p = token * top + j, e = choice[p]. moe_gemv_second: out[t, :] =
+// sum_j weight[t, j] * W_down,e_j hidden[t * top + j] (+ gate[t] * shared[t]) in float32, j in order.
+#define MV_THREADS 256
+#define MV_ROWS_PER_WARP 4
+
+template <typename T, bool VEC>
+__device__ __forceinline__ float mv_dot(const T* __restrict__ w, const float* __restrict__ x, int K, int lane) {
+    float s = 0.f;
+    if (VEC) {
+        for (int k = lane * 8; k < K; k += 256) {
+            float v[8];
+            load8(w + k, v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s = fmaf(v[e], x[k + e], s);
+        }
+    } else {
+        for (int k = lane; k < K; k += 32) s = fmaf(to_float(w[k]), x[k], s);
+    }
+    return warp_sum(s);
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(MV_THREADS)
+moe_gemv_first_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ W, long long w_expert_stride,
+                      const int* __restrict__ choice, int experts, int top, T* __restrict__ hidden, int N, int K,
+                      float limit, float alpha) {
+    extern __shared__ __align__(16) float mv_x[];          // [K]
+    pdl_wait();
+    pdl_launch_dependents();
+    const int p = blockIdx.y, e = choice[p];
+    const T* row = x + (size_t)(p / top) * ldx;
+    for (int k = threadIdx.x; k < K; k += MV_THREADS) mv_x[k] = to_float(row[k]);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n_begin = (blockIdx.x * (MV_THREADS / 32) + warp) * MV_ROWS_PER_WARP;
+    const bool valid = (unsigned)e < (unsigned)experts;
+    const T* We = W + (size_t)(valid ? e : 0) * w_expert_stride;
+    for (int n = n_begin; n < min(N, n_begin + MV_ROWS_PER_WARP); ++n) {
+        const float g = mv_dot<T, VEC>(We + (size_t)n * K, mv_x, K, lane);
+        const float u = mv_dot<T, VEC>(We + (size_t)(N + n) * K, mv_x, K, lane);
+        if (lane == 0) hidden[(size_t)p * N + n] = from_float<T>(valid ? glu_clamped(g, u, limit, alpha) : 0.f);
+    }
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(MV_THREADS)
+moe_gemv_second_kernel(const T* __restrict__ hidden, const T* __restrict__ W, long long w_expert_stride,
+                       const int* __restrict__ choice, const float* __restrict__ weight, int experts, int top,
+                       const T* __restrict__ shared_out, const float* __restrict__ shared_gate, float* __restrict__ out,
+                       int N, int K) {
+    extern __shared__ __align__(16) float mv_h[];          // [top, K]
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t = blockIdx.y;
+    for (int i = threadIdx.x; i < top * K; i += MV_THREADS) mv_h[i] = to_float(hidden[(size_t)t * top * K + i]);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n_begin = (blockIdx.x * (MV_THREADS / 32) + warp) * MV_ROWS_PER_WARP;
+    for (int n = n_begin; n < min(N, n_begin + MV_ROWS_PER_WARP); ++n) {
+        float acc = 0.f;
+        for (int j = 0; j < top; ++j) {
+            const int e = choice[(size_t)t * top + j];
+            if ((unsigned)e >= (unsigned)experts) continue;
+            const float d = mv_dot<T, VEC>(W + (size_t)e * w_expert_stride + (size_t)n * K, mv_h + (size_t)j * K, K, lane);
+            acc = fmaf(weight[(size_t)t * top + j], d, acc);
+        }
+        if (lane == 0) {
+            if (shared_out != nullptr) acc = fmaf(shared_gate[t], to_float(shared_out[(size_t)t * N + n]), acc);
+            out[(size_t)t * N + n] = acc;
+        }
+    }
+}
+
+// x [tokens, width]; w_gate_up [experts, 2 inter, width]; w_down [experts, width, inter]; hidden: scratch
+// [tokens * top, inter] of the compute type; out float32 [tokens, width]; shared_out of the compute type or null.
+TTB_EXPORT int ttb_moe_gemv(const void* x, int ldx, const void* w_gate_up, const void* w_down, const int* choice,
+                            const float* weight, void* hidden, const void* shared_out, const float* shared_gate, float* out,
+                            int dtype, int tokens, int experts, int top, int inter, int width, float limit, float alpha,
+                            cudaStream_t stream) {
+    if (tokens == 0) return TTB_OK;
+    if (!x || !w_gate_up || !w_down || !choice || !weight || !hidden || !out || (shared_out && !shared_gate)) return TTB_ERR_ARGUMENT;
+    const int pairs = tokens * top;
+    if (pairs > 65535) return TTB_ERR_UNSUPPORTED;
+    const size_t smem1 = (size_t)width * sizeof(float), smem2 = (size_t)top * inter * sizeof(float);
+    if (smem1 > 48 * 1024 || smem2 > 48 * 1024) return TTB_ERR_UNSUPPORTED;
+    const int per_block = (MV_THREADS / 32) * MV_ROWS_PER_WARP;
+    dim3 g1((inter + per_block - 1) / per_block, pairs), g2((width + per_block - 1) / per_block, tokens);
+    const long long s1 = 2LL * inter * width, s2 = (long long)width * inter;
+#define MV_LAUNCH(T, VEC)                                                                                            \
+    do {                                                                                                             \
+        ttb_launch(moe_gemv_first_kernel<T, VEC>, g1, MV_THREADS, smem1, stream, (const T*)x, ldx, (const T*)w_gate_up, s1, \
+                   choice, experts, top, (T*)hidden, inter, width, limit, alpha);                                    \
+        ttb_launch(moe_gemv_second_kernel<T, VEC>, g2, MV_THREADS, smem2, stream, (const T*)hidden, (const T*)w_down, s2,  \
+                   choice, weight, experts, top, (const T*)shared_out, shared_gate, out, width, inter);              \
+    } while (0)
+    const bool vec = (width & 7) == 0 && (inter & 7) == 0 && aligned32(w_gate_up) && aligned32(w_down);
+    if (dtype == TTB_DTYPE_BF16) { if (vec) MV_LAUNCH(__nv_bfloat16, true); else MV_LAUNCH(__nv_bfloat16, false); }
+    else if (dtype == TTB_DTYPE_F32) { if (vec) MV_LAUNCH(float, true); else MV_LAUNCH(float, false); }
+    else return TTB_ERR_UNSUPPORTED;
+#undef MV_LAUNCH
     return ttb_launch_status();
 }
 

@@ -96,7 +96,7 @@ class CudaKernels:
                      "ttb_gemv_ring", "ttb_gemm_skinny_tcgen05_qkv_rope", "ttb_add_layernorm", "ttb_latent_prepare",
                      "ttb_latent_attention_generic", "ttb_gate_heads", "ttb_gemm_simt_batched", "ttb_route_top",
                      "ttb_moe_align", "ttb_moe_group_gemm", "ttb_moe_combine", "ttb_glu_clamped",
-                     "ttb_latent_attention_mma", "ttb_latent_attention_mma_supports",
+                     "ttb_latent_attention_mma", "ttb_latent_attention_mma_supports", "ttb_moe_gemv",
                      "ttb_latent_attention_mma_tokens_per_tile"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
@@ -627,6 +627,7 @@ class CudaKernels:
             self._p(self.status), self._stream()), "latent_prepare")
         return cq
 
+    MOE_GEMV_PAIRS = 64          # up to this many (token, choice) pairs the experts run as matrix-vector products
     HEADS_LIBRARY_ROWS = 32      # per-head bfloat16 products with at least this many rows go to the library's batched product
 
     def heads_linear(self, x, w):
@@ -662,7 +663,7 @@ class CudaKernels:
             blocks = batch.num_segments * -(-batch.max_seg_len // per_tile) * -(-H // 64) * -(-R // 128)
             splits = 1
             if blocks < self.sm_count:
-                splits = max(1, min(-(-2 * self.sm_count // blocks), batch.max_context // 256, 64))
+                splits = max(1, min(-(-2 * self.sm_count // blocks), batch.max_context // 128, 64))
             partial_o = partial_ml = None
             if splits > 1:
                 partial_o = torch.empty(T * H * splits * R, dtype=torch.float32, device=self.device)
@@ -745,11 +746,22 @@ class CudaKernels:
         pairs = T * top
         if x.dtype != w_gate_up.dtype or x.stride(1) != 1 or not w_gate_up.is_contiguous() or not w_down.is_contiguous():
             raise KernelError("routed_experts: operands must share a dtype and be contiguous")
+        if shared_out is not None and (shared_out.shape != (T, width) or not shared_out.is_contiguous()):
+            raise KernelError("routed_experts: the shared expert's output must be contiguous [T, width]")
+        out = torch.empty(T, width, dtype=torch.float32, device=self.device)
+        hidden = torch.empty(pairs, inter, dtype=x.dtype, device=self.device)
+        if pairs <= self.MOE_GEMV_PAIRS and width * 4 <= 48 * 1024 and top * inter * 4 <= 48 * 1024:
+            # a handful of pairs (decode): every pair streams its expert's rows, no grouping
+            self._check(self.lib.ttb_moe_gemv(
+                self._p(x), x.stride(0), self._p(w_gate_up), self._p(w_down), self._p(choice), self._p(weight),
+                self._p(hidden), self._p(shared_out), self._p(shared_gate), self._p(out), _dtype_code(x.dtype), T, E, top,
+                inter, width, ctypes.c_float(limit), ctypes.c_float(alpha), self._stream()), "moe_gemv")
+            self.launches += 1
+            return out
         offsets = torch.empty(E + 1, dtype=torch.int32, device=self.device)
         order = torch.empty(pairs, dtype=torch.int32, device=self.device)
         self._check(self.lib.ttb_moe_align(self._p(choice), pairs, E, self._p(offsets), self._p(order), self._stream()),
                     "moe_align")
-        hidden = torch.empty(pairs, inter, dtype=x.dtype, device=self.device)
         code = _dtype_code(x.dtype)
         self._check(self.lib.ttb_moe_group_gemm(
             self._p(x), x.stride(0), self._p(w_gate_up), ctypes.c_longlong(two_inter * width), width, self._p(hidden), inter,
@@ -760,9 +772,6 @@ class CudaKernels:
             self._p(hidden), inter, self._p(w_down), ctypes.c_longlong(width * inter), inter, self._p(pair_out), width,
             code, 0, self._p(offsets), self._p(order), pairs, E, top, width, inter, ctypes.c_float(limit),
             ctypes.c_float(alpha), self._stream()), "moe_down")
-        out = torch.empty(T, width, dtype=torch.float32, device=self.device)
-        if shared_out is not None and (shared_out.shape != (T, width) or not shared_out.is_contiguous()):
-            raise KernelError("routed_experts: the shared expert's output must be contiguous [T, width]")
         self._check(self.lib.ttb_moe_combine(
             self._p(pair_out), self._p(weight), top, self._p(shared_out),
             _dtype_code(shared_out.dtype) if shared_out is not None else 0, self._p(shared_gate), self._p(out), T, width,
