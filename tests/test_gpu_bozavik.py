@@ -188,7 +188,8 @@ def test_latent_prepare_heads_linear_and_gate(kernels, twin, dtype, tol):
 
 # ---------------------------------------------------------------------------- the routed feed-forward
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 2e-5), (torch.bfloat16, 2e-2)])
-@pytest.mark.parametrize("T,width,E,top,inter", [(1, 64, 8, 2, 32), (7, 60, 5, 5, 20), (150, 128, 6, 3, 48), (40, 96, 1, 1, 72)])
+@pytest.mark.parametrize("T,width,E,top,inter", [(1, 64, 8, 2, 32), (7, 60, 5, 5, 20), (150, 128, 6, 3, 48), (40, 96, 1, 1, 72),
+                                                 (600, 128, 5, 2, 72), (520, 320, 3, 2, 136)])
 def test_router_and_experts_against_their_twins(kernels, twin, dtype, tol, T, width, E, top, inter):
     g = torch.Generator().manual_seed(T + E)
     x = torch.randn(T, width, generator=g).to(DEV, dtype)

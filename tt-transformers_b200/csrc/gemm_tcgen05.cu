@@ -21,6 +21,8 @@
 // own is in flight). Sizes: any M and N; K a multiple of 8 and row strides of 16 bytes (TMA).
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 #define TC_BM 128
@@ -390,4 +392,234 @@ TTB_EXPORT int ttb_gemm_tcgen05(const void* A, const void* W, void* C, int out_d
                    : tc_launch<true, __nv_bfloat16>(map_a, map_w, C, M, N, K, ldc, swiglu_rows, error_flag, stream);
     return f32 ? tc_launch<false, float>(map_a, map_w, C, M, N, K, ldc, 0, error_flag, stream)
                : tc_launch<false, __nv_bfloat16>(map_a, map_w, C, M, N, K, ldc, 0, error_flag, stream);
+}
+
+// ---------------------------------------------------------------------------- the same product over groups of rows
+// Routed experts: the rows of A lie expert by expert (offsets[e] .. offsets[e + 1]), expert e multiplies by its own
+// W_e (rows e * rows_per_expert .. of one stacked matrix). The grouping kernel leaves a table of row tiles
+// (expert, first row) and their count on the device, so no size is read back by the host; the grid is sized for the
+// most tiles there can be. A tile's box of 128 rows may reach into the next expert's rows: those rows are computed
+// and not stored. FIRST: W_e = [gate rows; up rows], the epilogue writes g' sigmoid(alpha g') (u' + 1) with
+// g' = min(g, L), u' = clamp(u, -L, L) into the hidden rows (grouped order). Otherwise: float32 results go to the
+// row that `sorted` names for each grouped row (the pair's own row).
+template <bool FIRST>
+__global__ void __launch_bounds__(TC_THREADS)
+moe_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                        void* __restrict__ out_raw, const int* __restrict__ offsets, const int* __restrict__ sorted,
+                        const int* __restrict__ tile_info, const int* __restrict__ num_m_tiles, int N, int K, int ldc,
+                        int rows_per_expert, int n_tiles, float limit, float alpha, int* __restrict__ error_flag) {
+    using Cfg = TcCfg;
+    using TO = typename std::conditional<FIRST, __nv_bfloat16, float>::type;
+    constexpr int OUT_COLS = FIRST ? Cfg::ACC_COLS / 2 : Cfg::ACC_COLS;
+    TO* out = reinterpret_cast<TO*>(out_raw);
+    extern __shared__ unsigned char tc_raw[];
+    unsigned char* tiles = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~(uintptr_t)1023);
+    unsigned char* staging = tiles + Cfg::STAGES * Cfg::STAGE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + Cfg::STAGING_BYTES);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * Cfg::STAGES + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int k_blocks = (K + TC_BK - 1) / TC_BK;
+    const uint32_t full0 = tc_smem(bars), empty0 = tc_smem(bars + Cfg::STAGES);
+    const uint32_t acc_full0 = tc_smem(bars + 2 * Cfg::STAGES), acc_empty0 = tc_smem(bars + 2 * Cfg::STAGES + 2);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(acc_full0 + 8 * a, 1);
+            mbar_init(acc_empty0 + 8 * a, 4);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(tc_smem(tmem_slot)), "r"((uint32_t)Cfg::TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();                       // A, the tile table and its count come from kernels before this one
+    const int m_tiles = *num_m_tiles;
+    const int num_tiles = m_tiles * n_tiles;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                const int mt = tile % m_tiles, n0 = (tile / m_tiles) * OUT_COLS;
+                const int expert = tile_info[2 * mt], row0 = tile_info[2 * mt + 1];
+                const int w_row = expert * rows_per_expert + n0;
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % Cfg::STAGES;
+                    const uint32_t round = it / Cfg::STAGES;
+                    if (round > 0 && !mbar_wait(empty0 + 8 * s, (round - 1) & 1)) {
+                        atomicExch(error_flag, TC_ERR_PRODUCER);
+                        tile = num_tiles;
+                        break;
+                    }
+                    const uint32_t bar = full0 + 8 * s;
+                    mbar_expect_tx(bar, Cfg::STAGE_BYTES);
+                    unsigned char* stage = tiles + s * Cfg::STAGE_BYTES;
+                    tma_load_2d(tc_smem(stage), &map_a, kb * TC_BK, row0, bar);
+                    if (FIRST) {
+                        tma_load_2d(tc_smem(stage + Cfg::A_BYTES), &map_w, kb * TC_BK, w_row, bar);
+                        tma_load_2d(tc_smem(stage + Cfg::A_BYTES + Cfg::B_BYTES / 2), &map_w, kb * TC_BK, w_row + N, bar);
+                    } else {
+                        tma_load_2d(tc_smem(stage + Cfg::A_BYTES), &map_w, kb * TC_BK, w_row, bar);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(Cfg::ACC_COLS >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+            uint32_t it = 0;
+            int local = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+                const int acc = local & 1;
+                if (local >= 2 && !mbar_wait(acc_empty0 + 8 * acc, ((local >> 1) - 1) & 1)) {
+                    atomicExch(error_flag, TC_ERR_MMA);
+                    break;
+                }
+                tc_fence_after();
+                bool ok = true;
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % Cfg::STAGES;
+                    if (!mbar_wait(full0 + 8 * s, (it / Cfg::STAGES) & 1)) {
+                        atomicExch(error_flag, TC_ERR_MMA);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = tc_smem(tiles + s * Cfg::STAGE_BYTES);
+                    const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < TC_BK / 16; ++k)
+                        tc_mma(tmem_base + acc * Cfg::ACC_COLS, tc_smem_desc(a_addr + k * 32), tc_smem_desc(b_addr + k * 32),
+                               idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    tc_commit(empty0 + 8 * s);
+                }
+                if (!ok) break;
+                tc_commit(acc_full0 + 8 * acc);
+            }
+        }
+    } else {
+        const int quarter = warp & 3;
+        constexpr int CHUNK_ELEMS = 16 / (int)sizeof(TO);
+        constexpr int LINE_COLS = 8 * CHUNK_ELEMS;
+        const bool vec = (ldc % CHUNK_ELEMS == 0) && (N % CHUNK_ELEMS == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+        uint4* stage_rows = reinterpret_cast<uint4*>(staging + quarter * 4096);
+        int local = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const int mt = tile % m_tiles, n0 = (tile / m_tiles) * OUT_COLS;
+            const int expert = tile_info[2 * mt];
+            const int row0 = tile_info[2 * mt + 1] + quarter * 32, row_end = offsets[expert + 1];
+            if (tile + (int)gridDim.x >= num_tiles) pdl_launch_dependents();
+            if (!mbar_wait(acc_full0 + 8 * acc, (local >> 1) & 1)) {
+                if (lane == 0) atomicExch(error_flag, TC_ERR_EPILOGUE);
+                break;
+            }
+            tc_fence_after();
+            // where this lane's row goes: the hidden rows keep the grouped order, results go to the pair's own row
+            const long long my_dst = row0 + lane < row_end ? (FIRST ? (long long)(row0 + lane) : (long long)sorted[row0 + lane]) : -1;
+            const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_COLS;
+#pragma unroll 1
+            for (int c0 = 0; c0 < OUT_COLS; c0 += LINE_COLS) {
+#pragma unroll
+                for (int h = 0; h < LINE_COLS / 32; ++h) {
+                    uint32_t accv[32];
+                    tc_load32(lane_addr + c0 + h * 32, accv);
+                    float v[32];
+                    if (FIRST) {
+                        uint32_t up[32];
+                        tc_load32(lane_addr + OUT_COLS + c0 + h * 32, up);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float g = fminf(__uint_as_float(accv[j]), limit);
+                            const float u = fminf(fmaxf(__uint_as_float(up[j]), -limit), limit);
+                            v[j] = __fdividef(g, 1.f + __expf(-alpha * g)) * (u + 1.f);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(accv[j]);
+                    }
+                    if (vec) {
+#pragma unroll
+                        for (int q = 0; q < 32 / CHUNK_ELEMS; ++q) {
+                            const int chunk = h * (32 / CHUNK_ELEMS) + q;
+                            stage_rows[lane * 8 + (chunk ^ (lane & 7))] = pack_chunk<TO>(v + q * CHUNK_ELEMS);
+                        }
+                    } else if (my_dst >= 0) {
+                        TO* dst = out + (size_t)my_dst * ldc + n0 + c0 + h * 32;
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + c0 + h * 32 + j < N) dst[j] = from_float<TO>(v[j]);
+                    }
+                }
+                if (vec) {
+                    __syncwarp();
+                    const int chunk = lane & 7, col = n0 + c0 + chunk * CHUNK_ELEMS;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int r = i * 4 + (lane >> 3);
+                        const uint4 value = stage_rows[r * 8 + (chunk ^ (r & 7))];
+                        const long long dst_row = __shfl_sync(0xffffffffu, my_dst, r);
+                        if (dst_row >= 0 && col < N)
+                            *reinterpret_cast<uint4*>(out + (size_t)dst_row * ldc + col) = value;
+                    }
+                    __syncwarp();
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acc_empty0 + 8 * acc) : "memory");
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)Cfg::TMEM_COLS) : "memory");
+    }
+}
+
+// A [rows, K] in grouped order; W [experts * rows_per_expert, K] (first: rows_per_expert = 2 N, gate then up rows;
+// otherwise N); C: first ? bfloat16 hidden [rows, N] : float32 [rows, N] written by `sorted`. tile_info / num_m_tiles:
+// what the grouping kernel left for row tiles of 128. max_m_tiles: the most row tiles there can be.
+TTB_EXPORT int ttb_moe_gemm_tcgen05(const void* A, int lda, const void* W, int ldw, void* C, int ldc, int first,
+                                    const int* offsets, const int* sorted, const int* tile_info, const int* num_m_tiles,
+                                    int rows, int experts, int max_m_tiles, int N, int K, float limit, float alpha,
+                                    int* error_flag, cudaStream_t stream) {
+    if (rows == 0 || N == 0) return TTB_OK;
+    if (!A || !W || !C || !offsets || !sorted || !tile_info || !num_m_tiles || !error_flag) return TTB_ERR_ARGUMENT;
+    if (K < 8 || (K & 7) || (lda & 7) || (ldw & 7) || !aligned16(A) || !aligned16(W)) return TTB_ERR_UNSUPPORTED;
+    const int rows_per_expert = first ? 2 * N : N;
+    if ((long long)experts * rows_per_expert > 2147483647LL) return TTB_ERR_UNSUPPORTED;
+    CUtensorMap map_a, map_w;
+    if (!tc_make_map(&map_a, A, rows, K, lda, TC_BM)) return TTB_ERR_UNSUPPORTED;
+    if (!tc_make_map(&map_w, W, experts * rows_per_expert, K, ldw, first ? TcCfg::ACC_COLS / 2 : TcCfg::ACC_COLS)) return TTB_ERR_UNSUPPORTED;
+    const int out_cols = first ? TcCfg::ACC_COLS / 2 : TcCfg::ACC_COLS;
+    const int n_tiles = (N + out_cols - 1) / out_cols;
+    const long long most = (long long)max_m_tiles * n_tiles;
+    const int blocks = most < tc_sm_count() ? (int)most : tc_sm_count();
+    static TtbOncePerDevice configured;
+    if (configured.pending()) {
+        cudaError_t e = cudaFuncSetAttribute(moe_gemm_tcgen05_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg::SMEM_BYTES);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(moe_gemm_tcgen05_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg::SMEM_BYTES);
+        if (e != cudaSuccess) return (int)e;
+        configured.mark();
+    }
+    if (first)
+        ttb_launch(moe_gemm_tcgen05_kernel<true>, dim3(blocks), dim3(TC_THREADS), (size_t)TcCfg::SMEM_BYTES, stream, map_a, map_w,
+                   C, offsets, sorted, tile_info, num_m_tiles, N, K, ldc, rows_per_expert, n_tiles, limit, alpha, error_flag);
+    else
+        ttb_launch(moe_gemm_tcgen05_kernel<false>, dim3(blocks), dim3(TC_THREADS), (size_t)TcCfg::SMEM_BYTES, stream, map_a, map_w,
+                   C, offsets, sorted, tile_info, num_m_tiles, N, K, ldc, rows_per_expert, n_tiles, limit, alpha, error_flag);
+    return ttb_launch_status();
 }

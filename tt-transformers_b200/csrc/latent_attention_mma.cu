@@ -86,33 +86,30 @@ latent_attention_mma_kernel(const LatentMmaArgs a) {
 
     // ---- the query tile: latent part as it is, rotated part rotated by the token's position
     const int lat_vecs = a.latent / 8;
-    for (int i = tid; i < LM_ROWS * lat_vecs; i += LM_THREADS) {
-        const int r = i / lat_vecs, c = (i % lat_vecs) * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < valid_rows) {
-            const size_t tok = seg_begin + tok_off0 + r / nh;
-            v = *reinterpret_cast<const uint4*>(a.q_lat + tok * a.ql_stride_t + (size_t)(h0 + r % nh) * a.ql_stride_h + c);
-        }
-        *reinterpret_cast<uint4*>(Qs + r * ldq + c) = v;
-    }
-    if (a.extra > 0) {
-        const int half = a.rotary_dim / 2;
-        for (int i = tid; i < LM_ROWS * a.extra; i += LM_THREADS) {
-            const int r = i / a.extra, d = i % a.extra;
-            float v = 0.f;
-            if (r < valid_rows) {
-                const size_t tok = seg_begin + tok_off0 + r / nh;
-                const __nv_bfloat16* src = a.q_rot + tok * a.qr_stride_t + (size_t)(h0 + r % nh) * a.qr_stride_h;
-                v = __bfloat162float(src[d]);
-                if (d < a.rotary_dim) {
-                    const int f = d < half ? d : d - half;
-                    float sn, cs;
-                    sincosf((float)(pos0 + r / nh) * a.inv_freq[f], &sn, &cs);
-                    const float other = __bfloat162float(src[d < half ? d + half : d - half]);
-                    v = d < half ? v * cs - other * sn : v * cs + other * sn;
+    for (int r = warp; r < LM_ROWS; r += LM_THREADS / 32) {
+        const bool row_valid = r < valid_rows;
+        const size_t tok = seg_begin + tok_off0 + (row_valid ? r / nh : 0);
+        const int h = h0 + (row_valid ? r % nh : 0);
+        const __nv_bfloat16* src = a.q_lat + tok * a.ql_stride_t + (size_t)h * a.ql_stride_h;
+        for (int c = lane; c < lat_vecs; c += 32)
+            *reinterpret_cast<uint4*>(Qs + r * ldq + c * 8) = row_valid ? *reinterpret_cast<const uint4*>(src + c * 8) : make_uint4(0, 0, 0, 0);
+        if (a.extra > 0) {
+            const int half = a.rotary_dim / 2;
+            const __nv_bfloat16* rsrc = a.q_rot + tok * a.qr_stride_t + (size_t)h * a.qr_stride_h;
+            for (int d = lane; d < a.extra; d += 32) {
+                float v = 0.f;
+                if (row_valid) {
+                    v = __bfloat162float(rsrc[d]);
+                    if (d < a.rotary_dim) {          // rotated by the token's position: pairs (i, i + rotary_dim / 2)
+                        const int f = d < half ? d : d - half;
+                        float sn, cs;
+                        sincosf((float)(pos0 + r / nh) * a.inv_freq[f], &sn, &cs);
+                        const float other = __bfloat162float(rsrc[d < half ? d + half : d - half]);
+                        v = d < half ? v * cs - other * sn : v * cs + other * sn;
+                    }
                 }
+                Qs[r * ldq + a.latent + d] = __float2bfloat16_rn(v);
             }
-            Qs[r * ldq + a.latent + d] = __float2bfloat16_rn(v);
         }
     }
 
@@ -138,19 +135,22 @@ latent_attention_mma_kernel(const LatentMmaArgs a) {
     // one key tile into shared memory: a warp per row, 16-byte copies that bypass the registers; rows past the last
     // visible key (and rows of pages outside the pool) become zeros
     auto fetch = [&](int kt, __nv_bfloat16* dst) {
-        for (int r = warp; r < LM_KEYS; r += LM_THREADS / 32) {
-            const int key = kt * LM_KEYS + r;
-            const __nv_bfloat16* src = a.rows;
-            int bytes = 0;
-            if (key <= last_key) {
+        // lane l looks up the row of key r = warp + 4 l for its warp (all lookups in flight together)
+        long long my_row = -1;
+        {
+            const int key = kt * LM_KEYS + warp + (LM_THREADS / 32) * lane;
+            if (lane < LM_KEYS / (LM_THREADS / 32) && key <= last_key) {
                 const int page = table[key / a.page_size];
-                if ((unsigned)page < (unsigned)a.num_pages) {
-                    src = a.rows + ((size_t)page * a.page_size + key % a.page_size) * dk;
-                    bytes = 16;
-                } else if (lane == 0) {
-                    atomicExch(a.status, 0x2000000 + seg_begin + tok_off0);
-                }
+                if ((unsigned)page < (unsigned)a.num_pages) my_row = (long long)page * a.page_size + key % a.page_size;
+                else atomicExch(a.status, 0x2000000 + seg_begin + tok_off0);
             }
+        }
+#pragma unroll 4
+        for (int i = 0; i < LM_KEYS / (LM_THREADS / 32); ++i) {
+            const long long row = __shfl_sync(0xffffffffu, my_row, i);
+            const int r = warp + (LM_THREADS / 32) * i;
+            const __nv_bfloat16* src = row >= 0 ? a.rows + (size_t)row * dk : a.rows;
+            const int bytes = row >= 0 ? 16 : 0;
             for (int c = lane; c < vecs; c += 32) cp_async16(dst + r * ldq + c * 8, bytes ? src + c * 8 : src, bytes);
         }
         cp_async_commit();
@@ -273,20 +273,35 @@ latent_attention_mma_kernel(const LatentMmaArgs a) {
 // out[row, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s, splits in their order.
 __global__ void latent_attention_merge_kernel(const float* __restrict__ partial_o, const float* __restrict__ partial_ml,
                                               __nv_bfloat16* __restrict__ out, int splits, int latent) {
+    __shared__ float wt[64];                  // 2^(m_s - M) / denominator, per split (at most 64 splits)
     pdl_wait();
     pdl_launch_dependents();
     const size_t row = blockIdx.x;
-    const float* ml = partial_ml + row * splits * 2;
-    float M = -INFINITY;
-    for (int s = 0; s < splits; ++s) M = fmaxf(M, ml[2 * s]);
-    float denom = 0.f;
-    for (int s = 0; s < splits; ++s) denom += ml[2 * s] == -INFINITY ? 0.f : exp2f(ml[2 * s] - M) * ml[2 * s + 1];
-    const float inv = denom > 0.f ? 1.f / denom : 0.f;
+    if (threadIdx.x < 32) {
+        const float2* ml = reinterpret_cast<const float2*>(partial_ml) + row * splits;
+        const int lane = threadIdx.x;
+        const float2 a = lane < splits ? ml[lane] : make_float2(-INFINITY, 0.f);
+        const float2 b = lane + 32 < splits ? ml[lane + 32] : make_float2(-INFINITY, 0.f);
+        const float M = warp_max(fmaxf(a.x, b.x));
+        const float wa = a.x == -INFINITY ? 0.f : exp2f(a.x - M), wb = b.x == -INFINITY ? 0.f : exp2f(b.x - M);
+        // the denominator in the order of the splits (one lane adds them up), so that it does not depend on the lanes' tree
+        wt[lane] = wa * a.y;
+        wt[lane + 32] = wb * b.y;
+        __syncwarp();
+        float denom = 0.f;
+        for (int s = 0; s < splits; ++s) denom += wt[s];
+        const float inv = denom > 0.f ? 1.f / denom : 0.f;
+        __syncwarp();
+        wt[lane] = wa * inv;
+        wt[lane + 32] = wb * inv;
+    }
+    __syncthreads();
     for (int c = threadIdx.x; c < latent; c += blockDim.x) {
+        const float* src = partial_o + row * splits * latent + c;
         float acc = 0.f;
-        for (int s = 0; s < splits; ++s)
-            if (ml[2 * s] != -INFINITY) acc += exp2f(ml[2 * s] - M) * partial_o[(row * splits + s) * latent + c];
-        out[row * latent + c] = __float2bfloat16_rn(acc * inv);
+#pragma unroll 8
+        for (int s = 0; s < splits; ++s) acc = fmaf(wt[s], src[(size_t)s * latent], acc);
+        out[row * latent + c] = __float2bfloat16_rn(acc);
     }
 }
 
@@ -318,7 +333,7 @@ TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t
     if (!ttb_latent_attention_mma_supports(latent, extra, rotary_dim, 0)) return TTB_ERR_UNSUPPORTED;
     if (extra > 0 && (!q_rot || (rotary_dim > 0 && !inv_freq))) return TTB_ERR_ARGUMENT;
     if ((ql_stride_t & 7) || (ql_stride_h & 7) || !aligned16(q_lat) || !aligned16(rows) || !aligned16(out)) return TTB_ERR_ARGUMENT;
-    if (splits < 1 || splits > 65535 || (splits > 1 && (!partial_o || !partial_ml))) return TTB_ERR_ARGUMENT;
+    if (splits < 1 || splits > 64 || (splits > 1 && (!partial_o || !partial_ml))) return TTB_ERR_ARGUMENT;
     LatentMmaArgs a;
     a.q_lat = (const __nv_bfloat16*)q_lat; a.ql_stride_t = ql_stride_t; a.ql_stride_h = ql_stride_h;
     a.q_rot = (const __nv_bfloat16*)q_rot; a.qr_stride_t = qr_stride_t; a.qr_stride_h = qr_stride_h;

@@ -18,24 +18,34 @@
 #define RT_MAX_EXPERTS 1024
 
 template <typename T>
-__global__ void __launch_bounds__(RT_THREADS)
+__global__ void __launch_bounds__(1024)
 route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_router, int width, int experts, int top,
                  int shared, int* __restrict__ choice, float* __restrict__ weight, float* __restrict__ shared_gate) {
-    extern __shared__ float rt_smem[];
+    extern __shared__ __align__(16) float rt_smem[];
     float* h = rt_smem;                   // [width]
-    float* z = rt_smem + width;           // [experts + 1]
+    float* z = rt_smem + ((width + 3) & ~3);           // [experts + 1]
     int* taken = reinterpret_cast<int*>(z + experts + 1);    // [experts]
     pdl_wait();
     pdl_launch_dependents();
     const int t = blockIdx.x;
-    for (int c = threadIdx.x; c < width; c += RT_THREADS) h[c] = to_float(x[(size_t)t * ldx + c]);
-    for (int e = threadIdx.x; e < experts; e += RT_THREADS) taken[e] = 0;
+    for (int c = threadIdx.x; c < width; c += blockDim.x) h[c] = to_float(x[(size_t)t * ldx + c]);
+    for (int e = threadIdx.x; e < experts; e += blockDim.x) taken[e] = 0;
     __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int e = warp; e < experts + (shared ? 1 : 0); e += RT_THREADS / 32) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const bool vec = (width & 3) == 0;
+    for (int e = warp; e < experts + (shared ? 1 : 0); e += nwarps) {
         const float* w = w_router + (size_t)e * width;
         float s = 0.f;
-        for (int c = lane; c < width; c += 32) s = fmaf(h[c], w[c], s);
+        if (vec) {          // all of a lane's loads are independent: they are in flight together
+#pragma unroll 8
+            for (int c = lane * 4; c < width; c += 128) {
+                const float4 a = *reinterpret_cast<const float4*>(w + c);
+                const float4 b = *reinterpret_cast<const float4*>(h + c);
+                s = fmaf(a.x, b.x, s); s = fmaf(a.y, b.y, s); s = fmaf(a.z, b.z, s); s = fmaf(a.w, b.w, s);
+            }
+        } else {
+            for (int c = lane; c < width; c += 32) s = fmaf(h[c], w[c], s);
+        }
         s = warp_sum(s);
         if (lane == 0) z[e] = s;
     }
@@ -81,13 +91,18 @@ TTB_EXPORT int ttb_route_top(const void* x, int dtype, int ldx, const float* w_r
     if (tokens == 0) return TTB_OK;
     if (!x || !w_router || !choice || !weight || (shared && !shared_gate)) return TTB_ERR_ARGUMENT;
     if (experts < 1 || experts > RT_MAX_EXPERTS || top < 1 || top > experts) return TTB_ERR_UNSUPPORTED;
-    const size_t smem = (size_t)(width + 2 * experts + 1) * sizeof(float);
+    const size_t smem = (size_t)(((width + 3) & ~3) + 2 * experts + 1) * sizeof(float);
     if (smem > 48 * 1024) return TTB_ERR_UNSUPPORTED;
+    const int rows = experts + (shared ? 1 : 0);
+    // a warp per logit, up to 32 warps for a handful of tokens (latency) and up to 8 for many (more blocks an SM)
+    const int most = tokens > 64 ? 8 : 32;
+    const int threads = 32 * (rows < 4 ? 4 : (rows > most ? most : rows));
+    if ((width & 3) == 0 && !aligned16(w_router)) return TTB_ERR_ARGUMENT;
     if (dtype == TTB_DTYPE_BF16)
-        ttb_launch(route_top_kernel<__nv_bfloat16>, tokens, RT_THREADS, smem, stream, (const __nv_bfloat16*)x, ldx, w_router,
+        ttb_launch(route_top_kernel<__nv_bfloat16>, tokens, threads, smem, stream, (const __nv_bfloat16*)x, ldx, w_router,
                    width, experts, top, shared, choice, weight, shared_gate);
     else if (dtype == TTB_DTYPE_F32)
-        ttb_launch(route_top_kernel<float>, tokens, RT_THREADS, smem, stream, (const float*)x, ldx, w_router, width, experts,
+        ttb_launch(route_top_kernel<float>, tokens, threads, smem, stream, (const float*)x, ldx, w_router, width, experts,
                    top, shared, choice, weight, shared_gate);
     else
         return TTB_ERR_UNSUPPORTED;
@@ -97,8 +112,11 @@ TTB_EXPORT int ttb_route_top(const void* x, int dtype, int ldx, const float* w_r
 // ---------------------------------------------------------------- grouping
 // offsets[e] .. offsets[e + 1]: where expert e's pairs lie in `sorted`; pairs of one expert in increasing order
 // of their index (token * top + choice rank), so the layout is the same whenever the choices are.
+#define AL_CHUNK 8192
 __global__ void __launch_bounds__(1024)
-moe_align_kernel(const int* __restrict__ choice, int pairs, int experts, int* __restrict__ offsets, int* __restrict__ sorted) {
+moe_align_kernel(const int* __restrict__ choice, int pairs, int experts, int top, int* __restrict__ offsets,
+                 int* __restrict__ sorted, int* __restrict__ sorted_token, int* __restrict__ tile_info,
+                 int* __restrict__ num_m_tiles, int tile_rows) {
     extern __shared__ int al_smem[];
     int* count = al_smem;                 // [experts + 1]
     pdl_wait();
@@ -119,26 +137,54 @@ moe_align_kernel(const int* __restrict__ choice, int pairs, int experts, int* __
             run += c;
         }
         offsets[experts] = run;
+        if (tile_info != nullptr) {           // row tiles of tile_rows rows, expert by expert: (expert, first row)
+            int tiles = 0;
+            for (int e = 0; e < experts; ++e)
+                for (int r = offsets[e]; r < offsets[e + 1]; r += tile_rows) {
+                    tile_info[2 * tiles] = e;
+                    tile_info[2 * tiles + 1] = r;
+                    ++tiles;
+                }
+            *num_m_tiles = tiles;
+        }
     }
     __syncthreads();
-    // one warp per expert walks the pairs in order and writes those of its expert (stable, no atomics)
+    // one warp per expert walks the pairs in order and writes those of its expert (stable, no atomics); the pairs
+    // pass through shared memory in chunks, so the walk does not wait on global memory
+    int* chunk = count + experts + 1;                     // [AL_CHUNK]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    for (int e = warp; e < experts; e += nwarps) {
-        int at = count[e];
-        for (int p0 = 0; p0 < pairs; p0 += 32) {
-            const int p = p0 + lane;
-            const bool mine = p < pairs && choice[p] == e;
-            const unsigned ballot = __ballot_sync(0xffffffffu, mine);
-            if (mine) sorted[at + __popc(ballot & ((1u << lane) - 1))] = p;
-            at += __popc(ballot);
+    for (int c0 = 0; c0 < pairs; c0 += AL_CHUNK) {
+        const int n = min(AL_CHUNK, pairs - c0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x) chunk[i] = choice[c0 + i];
+        __syncthreads();
+        for (int e = warp; e < experts; e += nwarps) {
+            int at = count[e];
+            for (int p0 = 0; p0 < n; p0 += 32) {
+                const int p = p0 + lane;
+                const bool mine = p < n && chunk[p] == e;
+                const unsigned ballot = __ballot_sync(0xffffffffu, mine);
+                if (mine) {
+                    const int slot = at + __popc(ballot & ((1u << lane) - 1));
+                    sorted[slot] = c0 + p;
+                    if (sorted_token != nullptr) sorted_token[slot] = (c0 + p) / top;
+                }
+                at += __popc(ballot);
+            }
+            if (lane == 0) count[e] = at;
         }
     }
 }
 
-TTB_EXPORT int ttb_moe_align(const int* choice, int pairs, int experts, int* offsets, int* sorted, cudaStream_t stream) {
+// sorted_token (the token of every grouped row), tile_info ((expert, first row) per row tile of tile_rows rows) and
+// num_m_tiles (their count) may be null.
+TTB_EXPORT int ttb_moe_align(const int* choice, int pairs, int experts, int top, int* offsets, int* sorted, int* sorted_token,
+                             int* tile_info, int* num_m_tiles, int tile_rows, cudaStream_t stream) {
     if (pairs == 0) return TTB_OK;
+    if (tile_info && (!num_m_tiles || tile_rows < 1)) return TTB_ERR_ARGUMENT;
     if (!choice || !offsets || !sorted || experts < 1 || experts > RT_MAX_EXPERTS) return TTB_ERR_ARGUMENT;
-    ttb_launch(moe_align_kernel, 1, 1024, (size_t)(experts + 1) * sizeof(int), stream, choice, pairs, experts, offsets, sorted);
+    ttb_launch(moe_align_kernel, 1, 1024, (size_t)(experts + 1 + AL_CHUNK) * sizeof(int), stream, choice, pairs, experts, top, offsets, sorted,
+               sorted_token, tile_info, num_m_tiles, tile_rows);
     return ttb_launch_status();
 }
 
@@ -430,20 +476,36 @@ TTB_EXPORT int ttb_moe_group_gemm(const void* A, int lda, const void* W, long lo
 #define MV_THREADS 256
 #define MV_ROWS_PER_WARP 4
 
-template <typename T, bool VEC>
-__device__ __forceinline__ float mv_dot(const T* __restrict__ w, const float* __restrict__ x, int K, int lane) {
-    float s = 0.f;
-    if (VEC) {
-        for (int k = lane * 8; k < K; k += 256) {
-            float v[8];
-            load8(w + k, v);
+// R dot products of one x (shared memory, float32) with R rows of W at once: the R loads of a step are independent
+// and in flight together. Rows are given by pointer; all lanes get all R sums.
+template <typename T, bool VEC, int R>
+__device__ __forceinline__ void mv_dots(const T* const (&w)[R], const float* __restrict__ x, int K, int lane, float (&out)[R]) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) s = fmaf(v[e], x[k + e], s);
+    for (int r = 0; r < R; ++r) out[r] = 0.f;
+    if (VEC) {
+#pragma unroll 2
+        for (int k = lane * 8; k < K; k += 256) {
+            float v[R][8];
+#pragma unroll
+            for (int r = 0; r < R; ++r) load8(w[r] + k, v[r]);
+            const float4 xa = *reinterpret_cast<const float4*>(x + k), xb = *reinterpret_cast<const float4*>(x + k + 4);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float s = out[r];
+                s = fmaf(v[r][0], xa.x, s); s = fmaf(v[r][1], xa.y, s); s = fmaf(v[r][2], xa.z, s); s = fmaf(v[r][3], xa.w, s);
+                s = fmaf(v[r][4], xb.x, s); s = fmaf(v[r][5], xb.y, s); s = fmaf(v[r][6], xb.z, s); s = fmaf(v[r][7], xb.w, s);
+                out[r] = s;
+            }
         }
     } else {
-        for (int k = lane; k < K; k += 32) s = fmaf(to_float(w[k]), x[k], s);
+        for (int k = lane; k < K; k += 32) {
+            const float xv = x[k];
+#pragma unroll
+            for (int r = 0; r < R; ++r) out[r] = fmaf(to_float(w[r][k]), xv, out[r]);
+        }
     }
-    return warp_sum(s);
+#pragma unroll
+    for (int r = 0; r < R; ++r) out[r] = warp_sum(out[r]);
 }
 
 template <typename T, bool VEC>
@@ -460,12 +522,24 @@ moe_gemv_first_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ W,
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int n_begin = (blockIdx.x * (MV_THREADS / 32) + warp) * MV_ROWS_PER_WARP;
+    if (n_begin >= N) return;
     const bool valid = (unsigned)e < (unsigned)experts;
     const T* We = W + (size_t)(valid ? e : 0) * w_expert_stride;
-    for (int n = n_begin; n < min(N, n_begin + MV_ROWS_PER_WARP); ++n) {
-        const float g = mv_dot<T, VEC>(We + (size_t)n * K, mv_x, K, lane);
-        const float u = mv_dot<T, VEC>(We + (size_t)(N + n) * K, mv_x, K, lane);
-        if (lane == 0) hidden[(size_t)p * N + n] = from_float<T>(valid ? glu_clamped(g, u, limit, alpha) : 0.f);
+    const T* rows[2 * MV_ROWS_PER_WARP];
+#pragma unroll
+    for (int i = 0; i < MV_ROWS_PER_WARP; ++i) {
+        const int n = min(n_begin + i, N - 1);             // rows past the end repeat the last one and are not stored
+        rows[2 * i] = We + (size_t)n * K;
+        rows[2 * i + 1] = We + (size_t)(N + n) * K;
+    }
+    float d[2 * MV_ROWS_PER_WARP];
+    mv_dots<T, VEC, 2 * MV_ROWS_PER_WARP>(rows, mv_x, K, lane, d);
+    if (lane < MV_ROWS_PER_WARP && n_begin + lane < N) {
+        float g = 0.f, u = 0.f;
+#pragma unroll
+        for (int i = 0; i < MV_ROWS_PER_WARP; ++i)
+            if (lane == i) { g = d[2 * i]; u = d[2 * i + 1]; }
+        hidden[(size_t)p * N + n_begin + lane] = from_float<T>(valid ? glu_clamped(g, u, limit, alpha) : 0.f);
     }
 }
 
@@ -483,18 +557,31 @@ moe_gemv_second_kernel(const T* __restrict__ hidden, const T* __restrict__ W, lo
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int n_begin = (blockIdx.x * (MV_THREADS / 32) + warp) * MV_ROWS_PER_WARP;
-    for (int n = n_begin; n < min(N, n_begin + MV_ROWS_PER_WARP); ++n) {
-        float acc = 0.f;
-        for (int j = 0; j < top; ++j) {
-            const int e = choice[(size_t)t * top + j];
-            if ((unsigned)e >= (unsigned)experts) continue;
-            const float d = mv_dot<T, VEC>(W + (size_t)e * w_expert_stride + (size_t)n * K, mv_h + (size_t)j * K, K, lane);
-            acc = fmaf(weight[(size_t)t * top + j], d, acc);
-        }
-        if (lane == 0) {
-            if (shared_out != nullptr) acc = fmaf(shared_gate[t], to_float(shared_out[(size_t)t * N + n]), acc);
-            out[(size_t)t * N + n] = acc;
-        }
+    if (n_begin >= N) return;
+    float acc[MV_ROWS_PER_WARP];
+#pragma unroll
+    for (int i = 0; i < MV_ROWS_PER_WARP; ++i) acc[i] = 0.f;
+    for (int j = 0; j < top; ++j) {
+        const int e = choice[(size_t)t * top + j];
+        if ((unsigned)e >= (unsigned)experts) continue;
+        const T* rows[MV_ROWS_PER_WARP];
+#pragma unroll
+        for (int i = 0; i < MV_ROWS_PER_WARP; ++i)
+            rows[i] = W + (size_t)e * w_expert_stride + (size_t)min(n_begin + i, N - 1) * K;
+        float d[MV_ROWS_PER_WARP];
+        mv_dots<T, VEC, MV_ROWS_PER_WARP>(rows, mv_h + (size_t)j * K, K, lane, d);
+        const float wj = weight[(size_t)t * top + j];
+#pragma unroll
+        for (int i = 0; i < MV_ROWS_PER_WARP; ++i) acc[i] = fmaf(wj, d[i], acc[i]);
+    }
+    if (lane < MV_ROWS_PER_WARP && n_begin + lane < N) {
+        float v = 0.f;
+#pragma unroll
+        for (int i = 0; i < MV_ROWS_PER_WARP; ++i)
+            if (lane == i) v = acc[i];
+        const int n = n_begin + lane;
+        if (shared_out != nullptr) v = fmaf(shared_gate[t], to_float(shared_out[(size_t)t * N + n]), v);
+        out[(size_t)t * N + n] = v;
     }
 }
 

@@ -96,7 +96,7 @@ class CudaKernels:
                      "ttb_gemv_ring", "ttb_gemm_skinny_tcgen05_qkv_rope", "ttb_add_layernorm", "ttb_latent_prepare",
                      "ttb_latent_attention_generic", "ttb_gate_heads", "ttb_gemm_simt_batched", "ttb_route_top",
                      "ttb_moe_align", "ttb_moe_group_gemm", "ttb_moe_combine", "ttb_glu_clamped",
-                     "ttb_latent_attention_mma", "ttb_latent_attention_mma_supports", "ttb_moe_gemv",
+                     "ttb_latent_attention_mma", "ttb_latent_attention_mma_supports", "ttb_moe_gemv", "ttb_moe_gemm_tcgen05",
                      "ttb_latent_attention_mma_tokens_per_tile"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
@@ -627,6 +627,7 @@ class CudaKernels:
             self._p(self.status), self._stream()), "latent_prepare")
         return cq
 
+    MOE_TCGEN05_PAIRS = 1024     # from this many pairs on the experts' products run on the grouped tcgen05 kernel
     MOE_GEMV_PAIRS = 64          # up to this many (token, choice) pairs the experts run as matrix-vector products
     HEADS_LIBRARY_ROWS = 32      # per-head bfloat16 products with at least this many rows go to the library's batched product
 
@@ -760,18 +761,39 @@ class CudaKernels:
             return out
         offsets = torch.empty(E + 1, dtype=torch.int32, device=self.device)
         order = torch.empty(pairs, dtype=torch.int32, device=self.device)
-        self._check(self.lib.ttb_moe_align(self._p(choice), pairs, E, self._p(offsets), self._p(order), self._stream()),
-                    "moe_align")
         code = _dtype_code(x.dtype)
-        self._check(self.lib.ttb_moe_group_gemm(
-            self._p(x), x.stride(0), self._p(w_gate_up), ctypes.c_longlong(two_inter * width), width, self._p(hidden), inter,
-            code, 1, self._p(offsets), self._p(order), pairs, E, top, inter, width, ctypes.c_float(limit),
-            ctypes.c_float(alpha), self._stream()), "moe_gate_up")
         pair_out = torch.empty(pairs, width, dtype=torch.float32, device=self.device)
-        self._check(self.lib.ttb_moe_group_gemm(
-            self._p(hidden), inter, self._p(w_down), ctypes.c_longlong(width * inter), inter, self._p(pair_out), width,
-            code, 0, self._p(offsets), self._p(order), pairs, E, top, width, inter, ctypes.c_float(limit),
-            ctypes.c_float(alpha), self._stream()), "moe_down")
+        grouped_tc = (x.dtype == torch.bfloat16 and self.use_tcgen05 is not False and pairs >= self.MOE_TCGEN05_PAIRS
+                      and width % 8 == 0 and inter % 8 == 0 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0)
+        if grouped_tc:
+            # many pairs (prompt portions): the tokens' rows are laid out expert by expert and both products run on
+            # the fifth-generation tensor cores over those groups; no size is read back by the host
+            max_tiles = -(-pairs // 128) + E
+            tokens_of = torch.empty(pairs, dtype=torch.int32, device=self.device)
+            tile_info = torch.empty(2 * max_tiles + 1, dtype=torch.int32, device=self.device)
+            self._check(self.lib.ttb_moe_align(self._p(choice), pairs, E, top, self._p(offsets), self._p(order),
+                                               self._p(tokens_of), self._p(tile_info[1:]), self._p(tile_info), 128,
+                                               self._stream()), "moe_align")
+            grouped = self.gather_rows(x, tokens_of)
+            self._check(self.lib.ttb_moe_gemm_tcgen05(
+                self._p(grouped), width, self._p(w_gate_up), width, self._p(hidden), inter, 1, self._p(offsets),
+                self._p(order), self._p(tile_info[1:]), self._p(tile_info), pairs, E, max_tiles, inter, width,
+                ctypes.c_float(limit), ctypes.c_float(alpha), self._p(self.tc_error), self._stream()), "moe_gate_up_tcgen05")
+            self._check(self.lib.ttb_moe_gemm_tcgen05(
+                self._p(hidden), inter, self._p(w_down), inter, self._p(pair_out), width, 0, self._p(offsets),
+                self._p(order), self._p(tile_info[1:]), self._p(tile_info), pairs, E, max_tiles, width, inter,
+                ctypes.c_float(limit), ctypes.c_float(alpha), self._p(self.tc_error), self._stream()), "moe_down_tcgen05")
+        else:
+            self._check(self.lib.ttb_moe_align(self._p(choice), pairs, E, top, self._p(offsets), self._p(order), None, None,
+                                               None, 0, self._stream()), "moe_align")
+            self._check(self.lib.ttb_moe_group_gemm(
+                self._p(x), x.stride(0), self._p(w_gate_up), ctypes.c_longlong(two_inter * width), width, self._p(hidden), inter,
+                code, 1, self._p(offsets), self._p(order), pairs, E, top, inter, width, ctypes.c_float(limit),
+                ctypes.c_float(alpha), self._stream()), "moe_gate_up")
+            self._check(self.lib.ttb_moe_group_gemm(
+                self._p(hidden), inter, self._p(w_down), ctypes.c_longlong(width * inter), inter, self._p(pair_out), width,
+                code, 0, self._p(offsets), self._p(order), pairs, E, top, width, inter, ctypes.c_float(limit),
+                ctypes.c_float(alpha), self._stream()), "moe_down")
         self._check(self.lib.ttb_moe_combine(
             self._p(pair_out), self._p(weight), top, self._p(shared_out),
             _dtype_code(shared_out.dtype) if shared_out is not None else 0, self._p(shared_gate), self._p(out), T, width,
