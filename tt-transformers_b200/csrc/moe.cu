@@ -110,9 +110,7 @@ TTB_EXPORT int ttb_route_top(const void* x, int dtype, int ldx, const float* w_r
 }
 
 // ---------------------------------------------------------------- grouping
-// offsets[e] .. offsets[e + 1]: where expert e's pairs lie in `sorted`; pairs of one expert in increasing order
-// of their index (token * top + choice rank), so the layout is the same whenever the choices are.
-#define AL_CHUNK 8192
+// offsets[e] .. offsets[e + 1]: where expert e's pairs (token * top + choice rank) lie in `sorted`.
 __global__ void __launch_bounds__(1024)
 moe_align_kernel(const int* __restrict__ choice, int pairs, int experts, int top, int* __restrict__ offsets,
                  int* __restrict__ sorted, int* __restrict__ sorted_token, int* __restrict__ tile_info,
@@ -129,50 +127,32 @@ moe_align_kernel(const int* __restrict__ choice, int pairs, int experts, int top
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        int run = 0;
+        int run = 0, tiles = 0;
         for (int e = 0; e < experts; ++e) {
             const int c = count[e];
             count[e] = run;
             offsets[e] = run;
-            run += c;
-        }
-        offsets[experts] = run;
-        if (tile_info != nullptr) {           // row tiles of tile_rows rows, expert by expert: (expert, first row)
-            int tiles = 0;
-            for (int e = 0; e < experts; ++e)
-                for (int r = offsets[e]; r < offsets[e + 1]; r += tile_rows) {
+            if (tile_info != nullptr)             // row tiles of tile_rows rows, expert by expert: (expert, first row)
+                for (int r = run; r < run + c; r += tile_rows) {
                     tile_info[2 * tiles] = e;
                     tile_info[2 * tiles + 1] = r;
                     ++tiles;
                 }
-            *num_m_tiles = tiles;
+            run += c;
         }
+        offsets[experts] = run;
+        if (tile_info != nullptr) *num_m_tiles = tiles;
     }
     __syncthreads();
-    // one warp per expert walks the pairs in order and writes those of its expert (stable, no atomics); the pairs
-    // pass through shared memory in chunks, so the walk does not wait on global memory
-    int* chunk = count + experts + 1;                     // [AL_CHUNK]
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    for (int c0 = 0; c0 < pairs; c0 += AL_CHUNK) {
-        const int n = min(AL_CHUNK, pairs - c0);
-        __syncthreads();
-        for (int i = threadIdx.x; i < n; i += blockDim.x) chunk[i] = choice[c0 + i];
-        __syncthreads();
-        for (int e = warp; e < experts; e += nwarps) {
-            int at = count[e];
-            for (int p0 = 0; p0 < n; p0 += 32) {
-                const int p = p0 + lane;
-                const bool mine = p < n && chunk[p] == e;
-                const unsigned ballot = __ballot_sync(0xffffffffu, mine);
-                if (mine) {
-                    const int slot = at + __popc(ballot & ((1u << lane) - 1));
-                    sorted[slot] = c0 + p;
-                    if (sorted_token != nullptr) sorted_token[slot] = (c0 + p) / top;
-                }
-                at += __popc(ballot);
-            }
-            if (lane == 0) count[e] = at;
-        }
+    // every pair takes the next free place of its expert's range (a counter per expert in shared memory). Which
+    // place a pair gets varies from run to run; no result depends on it, since every row of the products is
+    // computed from that row alone.
+    for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
+        const int e = choice[p];
+        if ((unsigned)e >= (unsigned)experts) continue;
+        const int slot = atomicAdd(&count[e], 1);
+        sorted[slot] = p;
+        if (sorted_token != nullptr) sorted_token[slot] = p / top;
     }
 }
 
@@ -183,7 +163,7 @@ TTB_EXPORT int ttb_moe_align(const int* choice, int pairs, int experts, int top,
     if (pairs == 0) return TTB_OK;
     if (tile_info && (!num_m_tiles || tile_rows < 1)) return TTB_ERR_ARGUMENT;
     if (!choice || !offsets || !sorted || experts < 1 || experts > RT_MAX_EXPERTS) return TTB_ERR_ARGUMENT;
-    ttb_launch(moe_align_kernel, 1, 1024, (size_t)(experts + 1 + AL_CHUNK) * sizeof(int), stream, choice, pairs, experts, top, offsets, sorted,
+    ttb_launch(moe_align_kernel, 1, 1024, (size_t)(experts + 1) * sizeof(int), stream, choice, pairs, experts, top, offsets, sorted,
                sorted_token, tile_info, num_m_tiles, tile_rows);
     return ttb_launch_status();
 }
