@@ -59,21 +59,19 @@ struct LatentMmaArgs {
     int latent, extra, rotary_dim;
     float scale_log2; const float* sinks; const float* inv_freq;
     int splits; float* partial_o; float* partial_ml; int* status;
+    int paired;      // a block takes two query tiles (one from each end of the segment) or one
     int stages;      // key tiles in shared memory at a time: 2 (the next one is fetched under the products) or 1
 };
 
-__global__ void __launch_bounds__(LM_THREADS)
-latent_attention_mma_kernel(const LatentMmaArgs a) {
+// One query tile of one segment against its share of the key tiles.
+__device__ __noinline__ void latent_attention_tile(const LatentMmaArgs& a, int seg, int tile_in_seg) {
     extern __shared__ __align__(16) unsigned char lm_smem[];
     const int dk = a.latent + a.extra, ldq = dk + 8, vecs = dk / 8;
     __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(lm_smem);      // [LM_ROWS][ldq]
     __nv_bfloat16* Ks = Qs + LM_ROWS * ldq;                              // [LM_KEYS][ldq]
-    pdl_wait();
-    // the tiles at the end of a segment see the most keys: they start first
-    const int seg = blockIdx.x % a.segments, tile_in_seg = a.tiles_per_seg - 1 - blockIdx.x / a.segments;
     const int seg_begin = a.cu_seqlens[seg], seg_len = a.cu_seqlens[seg + 1] - seg_begin;
     const int tok_off0 = tile_in_seg * a.tokens_per_tile;
-    if (tok_off0 >= seg_len) { pdl_launch_dependents(); return; }
+    if (tok_off0 >= seg_len) return;
     const int ntok = min(a.tokens_per_tile, seg_len - tok_off0);
     const int pos0 = a.seg_pos0[seg] + tok_off0;            // position of the tile's first token
     const int hgroup = blockIdx.y / a.chunks, chunk = blockIdx.y % a.chunks;
@@ -166,18 +164,20 @@ latent_attention_mma_kernel(const LatentMmaArgs a) {
             cp_async_wait<0>();
         }
         __syncthreads();                                     // the tile (and, first, the query tile) is in place
+        if (warp * 16 < valid_rows) {          // a warp whose 16 rows are all idle only helps to fetch
         float s[LM_KEYS / 8][4];
 #pragma unroll
         for (int j = 0; j < LM_KEYS / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
         for (int k0 = 0; k0 < dk; k0 += 16) {
-            uint32_t qa[4];
+            uint32_t qa[4], kb[LM_KEYS / 16][4];
             ldsm_x4(qa, Qs + (warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ldq + k0 + (lane >> 4) * 8);
 #pragma unroll
+            for (int jp = 0; jp < LM_KEYS / 16; ++jp)          // all loads of the step first: they are in flight together
+                ldsm_x4(kb[jp], Kt + (jp * 16 + (lane & 7) + (lane >> 4) * 8) * ldq + k0 + ((lane >> 3) & 1) * 8);
+#pragma unroll
             for (int jp = 0; jp < LM_KEYS / 16; ++jp) {
-                uint32_t kb[4];
-                ldsm_x4(kb, Kt + (jp * 16 + (lane & 7) + (lane >> 4) * 8) * ldq + k0 + ((lane >> 3) & 1) * 8);
-                mma_bf16(s[2 * jp], qa, kb[0], kb[1]);
-                mma_bf16(s[2 * jp + 1], qa, kb[2], kb[3]);
+                mma_bf16(s[2 * jp], qa, kb[jp][0], kb[jp][1]);
+                mma_bf16(s[2 * jp + 1], qa, kb[jp][2], kb[jp][3]);
             }
         }
         // scale, mask, running maximum
@@ -226,19 +226,26 @@ latent_attention_mma_kernel(const LatentMmaArgs a) {
             pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
             pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
-            for (int np = 0; np < LM_CHUNK / 16; ++np) {
-                if (np * 16 < ncols) {
-                    uint32_t vb[4];
-                    ldsm_x4_trans(vb, Kt + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ldq + col0 + np * 16 + (lane >> 4) * 8);
-                    mma_bf16(o[2 * np], pa, vb[0], vb[1]);
-                    mma_bf16(o[2 * np + 1], pa, vb[2], vb[3]);
+            for (int np0 = 0; np0 < LM_CHUNK / 16; np0 += 4) {          // four loads in flight, then their eight products
+                if (np0 * 16 < ncols) {
+                    uint32_t vb[4][4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if ((np0 + i) * 16 < ncols)
+                            ldsm_x4_trans(vb[i], Kt + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ldq + col0 + (np0 + i) * 16 + (lane >> 4) * 8);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if ((np0 + i) * 16 < ncols) {
+                            mma_bf16(o[2 * (np0 + i)], pa, vb[i][0], vb[i][1]);
+                            mma_bf16(o[2 * (np0 + i) + 1], pa, vb[i][2], vb[i][3]);
+                        }
                 }
             }
+        }
         }
         __syncthreads();                                     // all warps are done with this tile: it may be overwritten
         if (a.stages == 1 && kt + 1 < kt_end) fetch(kt + 1, Ks);
     }
-    pdl_launch_dependents();
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
@@ -268,6 +275,21 @@ latent_attention_mma_kernel(const LatentMmaArgs a) {
             }
         }
     }
+}
+
+// A block takes a query tile from the end of its segment (many keys) and then its partner from the start (few), so
+// that all blocks of a long prompt portion walk about the same number of key tiles.
+__global__ void __launch_bounds__(LM_THREADS)
+latent_attention_mma_kernel(const LatentMmaArgs a) {
+    pdl_wait();
+    const int seg = blockIdx.x % a.segments, b = blockIdx.x / a.segments;
+    const int first = a.tiles_per_seg - 1 - b, second = a.paired ? b : first;
+    latent_attention_tile(a, seg, first);
+    if (second != first) {
+        __syncthreads();                      // the first tile's queries are no longer read
+        latent_attention_tile(a, seg, second);
+    }
+    pdl_launch_dependents();
 }
 
 // out[row, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s, splits in their order.
@@ -303,6 +325,13 @@ __global__ void latent_attention_merge_kernel(const float* __restrict__ partial_
         for (int s = 0; s < splits; ++s) acc = fmaf(wt[s], src[(size_t)s * latent], acc);
         out[row * latent + c] = __float2bfloat16_rn(acc);
     }
+}
+
+static int tc_like_sm_count() {
+    int device = 0, count = 0;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+    return count > 0 ? count : 1;
 }
 
 TTB_EXPORT int ttb_latent_attention_mma_supports(int latent, int extra, int rotary_dim, int window) {
@@ -348,7 +377,9 @@ TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t
     a.latent = latent; a.extra = extra; a.rotary_dim = rotary_dim;
     a.scale_log2 = scale * 1.4426950408889634f; a.sinks = sinks; a.inv_freq = inv_freq;
     a.splits = splits; a.partial_o = partial_o; a.partial_ml = partial_ml; a.status = status;
-    const long long blocks_x = (long long)segments * a.tiles_per_seg;
+    // with blocks in plenty a block takes a long tile and its short partner (even work); else one tile, longest first
+    a.paired = (long long)segments * a.tiles_per_seg >= 16LL * tc_like_sm_count();
+    const long long blocks_x = (long long)segments * (a.paired ? (a.tiles_per_seg + 1) / 2 : a.tiles_per_seg);
     const int groups = (heads + a.heads_per_group - 1) / a.heads_per_group;
     if (blocks_x > 2147483647LL || groups * a.chunks > 65535) return TTB_ERR_UNSUPPORTED;
     const size_t tile_bytes = (size_t)LM_KEYS * (latent + extra + 8) * 2;
