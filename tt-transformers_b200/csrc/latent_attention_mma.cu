@@ -36,6 +36,12 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// 2^x in one instruction (exp2f adds range handling around it); 2^-inf = 0
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&v);
@@ -64,7 +70,7 @@ struct LatentMmaArgs {
 };
 
 // One query tile of one segment against its share of the key tiles.
-__device__ __noinline__ void latent_attention_tile(const LatentMmaArgs& a, int seg, int tile_in_seg) {
+__device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, int seg, int tile_in_seg) {
     extern __shared__ __align__(16) unsigned char lm_smem[];
     const int dk = a.latent + a.extra, ldq = dk + 8, vecs = dk / 8;
     __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(lm_smem);      // [LM_ROWS][ldq]
@@ -198,16 +204,16 @@ __device__ __noinline__ void latent_attention_tile(const LatentMmaArgs& a, int s
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
         const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
         const float base0 = n0 == -INFINITY ? 0.f : n0, base1 = n1 == -INFINITY ? 0.f : n1;
-        const float corr0 = exp2f(m0 - base0), corr1 = exp2f(m1 - base1);     // exp2(-inf) = 0
+        const float corr0 = fast_exp2(m0 - base0), corr1 = fast_exp2(m1 - base1);     // exp2(-inf) = 0
         m0 = n0;
         m1 = n1;
         float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
         for (int j = 0; j < LM_KEYS / 8; ++j) {
-            s[j][0] = exp2f(s[j][0] - base0);
-            s[j][1] = exp2f(s[j][1] - base0);
-            s[j][2] = exp2f(s[j][2] - base1);
-            s[j][3] = exp2f(s[j][3] - base1);
+            s[j][0] = fast_exp2(s[j][0] - base0);
+            s[j][1] = fast_exp2(s[j][1] - base0);
+            s[j][2] = fast_exp2(s[j][2] - base1);
+            s[j][3] = fast_exp2(s[j][3] - base1);
             sum0 += s[j][0] + s[j][1];
             sum1 += s[j][2] + s[j][3];
         }
