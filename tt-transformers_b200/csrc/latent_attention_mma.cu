@@ -31,6 +31,14 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
 }
+__device__ __forceinline__ void ldsm_x4_u32(uint32_t (&r)[4], uint32_t a) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_trans_u32(uint32_t (&r)[4], uint32_t a) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
 __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -136,35 +144,42 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
 #pragma unroll
     for (int j = 0; j < LM_CHUNK / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 
-    // one key tile into shared memory: a warp per row, 16-byte copies that bypass the registers; rows past the last
-    // visible key (and rows of pages outside the pool) become zeros
-    auto fetch = [&](int kt, __nv_bfloat16* dst) {
-        // lane l looks up the row of key r = warp + 4 l for its warp (all lookups in flight together)
-        long long my_row = -1;
-        {
-            const int key = kt * LM_KEYS + warp + (LM_THREADS / 32) * lane;
-            if (lane < LM_KEYS / (LM_THREADS / 32) && key <= last_key) {
-                const int page = table[key / a.page_size];
-                if ((unsigned)page < (unsigned)a.num_pages) my_row = (long long)page * a.page_size + key % a.page_size;
-                else atomicExch(a.status, 0x2000000 + seg_begin + tok_off0);
+    // one key tile into shared memory: two threads per row, each copies its half of the row in 16-byte pieces that
+    // bypass the registers; rows past the last visible key (and rows of pages outside the pool) become zeros
+    const int frow = tid >> 1, fhalf_off = (tid & 1) * (vecs >> 1) * 8, fvecs = vecs >> 1;
+    const uint32_t qs_u32 = (uint32_t)__cvta_generic_to_shared(Qs), ks_u32 = (uint32_t)__cvta_generic_to_shared(Ks);
+    auto fetch = [&](int kt, uint32_t dst_u32) {
+        const int key = kt * LM_KEYS + frow;
+        const __nv_bfloat16* src = a.rows;
+        int bytes = 0;
+        if (key <= last_key) {
+            const int page = table[key / a.page_size];
+            if ((unsigned)page < (unsigned)a.num_pages) {
+                src = a.rows + ((size_t)page * a.page_size + key % a.page_size) * dk + fhalf_off;
+                bytes = 16;
+            } else {
+                atomicExch(a.status, 0x2000000 + seg_begin + tok_off0);
             }
         }
-#pragma unroll 4
-        for (int i = 0; i < LM_KEYS / (LM_THREADS / 32); ++i) {
-            const long long row = __shfl_sync(0xffffffffu, my_row, i);
-            const int r = warp + (LM_THREADS / 32) * i;
-            const __nv_bfloat16* src = row >= 0 ? a.rows + (size_t)row * dk : a.rows;
-            const int bytes = row >= 0 ? 16 : 0;
-            for (int c = lane; c < vecs; c += 32) cp_async16(dst + r * ldq + c * 8, bytes ? src + c * 8 : src, bytes);
+        const uint32_t dst = dst_u32 + (uint32_t)(frow * ldq + fhalf_off) * 2;
+        for (int c = 0; c < fvecs; ++c) {
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + c * 16), "l"(bytes ? src + c * 8 : src), "r"(bytes) : "memory");
         }
         cp_async_commit();
     };
-    const int second = a.stages == 2 ? LM_KEYS * ldq : 0;      // offset of the second key buffer (none: the same one)
-    if (kt_begin < kt_end) fetch(kt_begin, Ks);
+    const uint32_t second = a.stages == 2 ? (uint32_t)(LM_KEYS * ldq * 2) : 0u;     // byte offset of the second key buffer
+    // shared-memory addresses of this lane's fragment rows, computed once
+    const uint32_t q_frag = qs_u32 + (uint32_t)((warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ldq + (lane >> 4) * 8) * 2;
+    const uint32_t k_frag = (uint32_t)(((lane & 7) + (lane >> 4) * 8) * ldq + ((lane >> 3) & 1) * 8) * 2;
+    const uint32_t v_frag = (uint32_t)(((lane & 7) + ((lane >> 3) & 1) * 8) * ldq + col0 + (lane >> 4) * 8) * 2;
+    const uint32_t rows16 = (uint32_t)(16 * ldq * 2);
+    // rows of this warp that see every key of a tile need no mask for it
+    const int warp_min_pos = (warp * 16 + 16 <= valid_rows) ? pos0 + (warp * 16) / nh : -1;
+    if (kt_begin < kt_end) fetch(kt_begin, ks_u32);
     for (int kt = kt_begin; kt < kt_end; ++kt) {
-        const __nv_bfloat16* Kt = Ks + ((kt - kt_begin) & 1) * second;
+        const uint32_t kt_u32 = ks_u32 + ((kt - kt_begin) & 1) * second;
         if (a.stages == 2 && kt + 1 < kt_end) {
-            fetch(kt + 1, Ks + ((kt + 1 - kt_begin) & 1) * second);     // lands while this tile is multiplied
+            fetch(kt + 1, ks_u32 + ((kt + 1 - kt_begin) & 1) * second);     // lands while this tile is multiplied
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
@@ -176,25 +191,29 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
         for (int j = 0; j < LM_KEYS / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
         for (int k0 = 0; k0 < dk; k0 += 16) {
             uint32_t qa[4], kb[LM_KEYS / 16][4];
-            ldsm_x4(qa, Qs + (warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ldq + k0 + (lane >> 4) * 8);
+            ldsm_x4_u32(qa, q_frag + k0 * 2);
 #pragma unroll
-            for (int jp = 0; jp < LM_KEYS / 16; ++jp)          // all loads of the step first: they are in flight together
-                ldsm_x4(kb[jp], Kt + (jp * 16 + (lane & 7) + (lane >> 4) * 8) * ldq + k0 + ((lane >> 3) & 1) * 8);
+            for (int jp = 0; jp < LM_KEYS / 16; ++jp) ldsm_x4_u32(kb[jp], kt_u32 + k_frag + jp * rows16 + k0 * 2);
 #pragma unroll
             for (int jp = 0; jp < LM_KEYS / 16; ++jp) {
                 mma_bf16(s[2 * jp], qa, kb[jp][0], kb[jp][1]);
                 mma_bf16(s[2 * jp + 1], qa, kb[jp][2], kb[jp][3]);
             }
         }
-        // scale, mask, running maximum
+        // mask (only tiles that reach past a row's position), running maximum of the raw scores
+        if (kt * LM_KEYS + LM_KEYS - 1 > warp_min_pos) {
+#pragma unroll
+            for (int j = 0; j < LM_KEYS / 8; ++j) {
+                const int key = kt * LM_KEYS + 8 * j + 2 * t4;
+                if (key > row_pos0) s[j][0] = -INFINITY;
+                if (key + 1 > row_pos0) s[j][1] = -INFINITY;
+                if (key > row_pos1) s[j][2] = -INFINITY;
+                if (key + 1 > row_pos1) s[j][3] = -INFINITY;
+            }
+        }
         float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
         for (int j = 0; j < LM_KEYS / 8; ++j) {
-            const int key = kt * LM_KEYS + 8 * j + 2 * t4;
-            s[j][0] = key <= row_pos0 ? s[j][0] * a.scale_log2 : -INFINITY;
-            s[j][1] = key + 1 <= row_pos0 ? s[j][1] * a.scale_log2 : -INFINITY;
-            s[j][2] = key <= row_pos1 ? s[j][2] * a.scale_log2 : -INFINITY;
-            s[j][3] = key + 1 <= row_pos1 ? s[j][3] * a.scale_log2 : -INFINITY;
             mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
             mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
         }
@@ -202,26 +221,29 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+        // the scale (positive) goes into the exponent: p = 2^(s * scale - maximum)
+        const float n0 = fmaxf(m0, mx0 * a.scale_log2), n1 = fmaxf(m1, mx1 * a.scale_log2);
         const float base0 = n0 == -INFINITY ? 0.f : n0, base1 = n1 == -INFINITY ? 0.f : n1;
-        const float corr0 = fast_exp2(m0 - base0), corr1 = fast_exp2(m1 - base1);     // exp2(-inf) = 0
+        const float corr0 = fast_exp2(m0 - base0), corr1 = fast_exp2(m1 - base1);     // 2^-inf = 0
         m0 = n0;
         m1 = n1;
         float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
         for (int j = 0; j < LM_KEYS / 8; ++j) {
-            s[j][0] = fast_exp2(s[j][0] - base0);
-            s[j][1] = fast_exp2(s[j][1] - base0);
-            s[j][2] = fast_exp2(s[j][2] - base1);
-            s[j][3] = fast_exp2(s[j][3] - base1);
+            s[j][0] = fast_exp2(fmaf(s[j][0], a.scale_log2, -base0));
+            s[j][1] = fast_exp2(fmaf(s[j][1], a.scale_log2, -base0));
+            s[j][2] = fast_exp2(fmaf(s[j][2], a.scale_log2, -base1));
+            s[j][3] = fast_exp2(fmaf(s[j][3], a.scale_log2, -base1));
             sum0 += s[j][0] + s[j][1];
             sum1 += s[j][2] + s[j][3];
         }
         l0 = l0 * corr0 + sum0;
         l1 = l1 * corr1 + sum1;
+        if (__any_sync(0xffffffffu, corr0 != 1.f || corr1 != 1.f)) {       // the maximum moved somewhere in the warp
 #pragma unroll
-        for (int j = 0; j < LM_CHUNK / 8; ++j) {
-            o[j][0] *= corr0; o[j][1] *= corr0; o[j][2] *= corr1; o[j][3] *= corr1;
+            for (int j = 0; j < LM_CHUNK / 8; ++j) {
+                o[j][0] *= corr0; o[j][1] *= corr0; o[j][2] *= corr1; o[j][3] *= corr1;
+            }
         }
         // O += P C: the values are the latent part of the key rows
 #pragma unroll
@@ -237,8 +259,7 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
                     uint32_t vb[4][4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
-                        if ((np0 + i) * 16 < ncols)
-                            ldsm_x4_trans(vb[i], Kt + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * ldq + col0 + (np0 + i) * 16 + (lane >> 4) * 8);
+                        if ((np0 + i) * 16 < ncols) ldsm_x4_trans_u32(vb[i], kt_u32 + v_frag + kk * rows16 + (np0 + i) * 32);
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
                         if ((np0 + i) * 16 < ncols) {
@@ -250,7 +271,7 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
         }
         }
         __syncthreads();                                     // all warps are done with this tile: it may be overwritten
-        if (a.stages == 1 && kt + 1 < kt_end) fetch(kt + 1, Ks);
+        if (a.stages == 1 && kt + 1 < kt_end) fetch(kt + 1, ks_u32);
     }
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -365,7 +386,7 @@ TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t
                                         cudaStream_t stream) {
     if (tokens == 0 || segments == 0) return TTB_OK;
     if (!q_lat || !out || !cu_seqlens || !seg_pos0 || !rows || !block_table || !status) return TTB_ERR_ARGUMENT;
-    if (!ttb_latent_attention_mma_supports(latent, extra, rotary_dim, 0)) return TTB_ERR_UNSUPPORTED;
+    if (!ttb_latent_attention_mma_supports(latent, extra, rotary_dim, 0) || !(scale > 0.f)) return TTB_ERR_UNSUPPORTED;
     if (extra > 0 && (!q_rot || (rotary_dim > 0 && !inv_freq))) return TTB_ERR_ARGUMENT;
     if ((ql_stride_t & 7) || (ql_stride_h & 7) || !aligned16(q_lat) || !aligned16(rows) || !aligned16(out)) return TTB_ERR_ARGUMENT;
     if (splits < 1 || splits > 64 || (splits > 1 && (!partial_o || !partial_ml))) return TTB_ERR_ARGUMENT;

@@ -656,7 +656,7 @@ class CudaKernels:
         if (q_rot is None) != (view.extra == 0) or (q_rot is not None and (q_rot.shape[2] != view.extra or q_rot.stride(2) != 1)):
             raise KernelError("latent_attention: the rotated query part does not fit the cache rows")
         out = torch.empty(T, H, R, dtype=q_latent.dtype, device=self.device)
-        if (self.use_mma_latent_attention and q_latent.dtype == torch.bfloat16 and view.rows.is_contiguous()
+        if (self.use_mma_latent_attention and q_latent.dtype == torch.bfloat16 and view.rows.is_contiguous() and scale > 0
                 and q_latent.stride(0) % 8 == 0 and q_latent.stride(1) % 8 == 0 and q_latent.data_ptr() % 16 == 0
                 and self.lib.ttb_latent_attention_mma_supports(R, view.extra, int(rotary_dim), int(view.window or 0))):
             # tensor cores; few blocks (decode): the keys are split over blocks and merged afterwards
