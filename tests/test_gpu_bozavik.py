@@ -96,7 +96,7 @@ def _latent_setup(segs, H, R, extra, rotary_dim, page, dtype, seed, shuffle_page
 
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 2e-5), (torch.bfloat16, 2e-2)])
 @pytest.mark.parametrize("H,R,extra,rotary_dim,page", [(6, 96, 0, 0, 16), (4, 128, 32, 32, 16), (5, 40, 12, 8, 4),
-                                                       (1, 20, 0, 0, 8), (70, 32, 16, 16, 16), (3, 272, 16, 16, 32)])
+                                                       (1, 20, 0, 0, 8), (70, 32, 16, 16, 16), (3, 272, 16, 16, 32), (2, 528, 0, 0, 16)])
 def test_latent_attention_against_its_twin(kernels, twin, dtype, tol, H, R, extra, rotary_dim, page):
     # a prompt portion beside cached tokens, decoded tokens at short and long contexts, a first token, and
     # portions that end just before, on and just after the edges of pages and of key tiles
@@ -113,6 +113,18 @@ def test_latent_attention_against_its_twin(kernels, twin, dtype, tol, H, R, extr
                 _close(kernels.latent_attention(q_lat, q_rot, batch, view, 0.2, use_sinks, inv_freq, rotary_dim), ref, tol)
             finally:
                 kernels.use_mma_latent_attention = True
+    # the mixer's end in one call (key splits merged, W_uv per head, gate), with few tokens and with many
+    g = torch.Generator().manual_seed(3)
+    for V, gate_cols in ((16, H), (24, H * 24), (8, 0)):
+        w_uv = (torch.randn(H, V, R, generator=g) * R ** -0.5).to(DEV, dtype)
+        gate = torch.randn(batch.num_tokens, gate_cols, generator=g).to(DEV) if gate_cols else None
+        for rows_limit in (1000, 0):
+            kernels.LATENT_OUT_ROWS, keep = rows_limit, kernels.LATENT_OUT_ROWS
+            try:
+                got_out = kernels.latent_attention_out(q_lat, q_rot, batch, view, 0.2, sinks, inv_freq, rotary_dim, w_uv, gate)
+            finally:
+                kernels.LATENT_OUT_ROWS = keep
+            _close(got_out, twin.latent_attention_out(q_lat, q_rot, batch, view, 0.2, sinks, inv_freq, rotary_dim, w_uv, gate), tol)
     with_sink = kernels.latent_attention(q_lat, q_rot, batch, view, 0.2, sinks + 3.0, inv_freq, rotary_dim)
     assert float((with_sink.float() - got.float()).abs().max()) > 0.05       # a sink that is left out shows
 
@@ -133,6 +145,11 @@ def test_one_key_far_away_carries_the_weight(kernels, dtype, far):
         got = kernels.latent_attention(q_lat, q_rot, batch, view, 1.0, None, inv_freq, 16)[-1].float()
         for h in range(H):
             assert float((got[h] - target).abs().max()) < 0.05, (segs, h)
+        # the same through the mixer's fused end (key splits merged inside it), W_uv the identity
+        eye = torch.eye(R, device=DEV, dtype=dtype).expand(H, R, R).contiguous()
+        fused = kernels.latent_attention_out(q_lat, q_rot, batch, view, 1.0, None, inv_freq, 16, eye, None)[-1].float().view(H, R)
+        for h in range(H):
+            assert float((fused[h] - target).abs().max()) < 0.05, (segs, h, "fused")
 
 
 def test_a_window_edge_in_the_general_kernel(kernels, twin):
@@ -210,6 +227,16 @@ def test_router_and_experts_against_their_twins(kernels, twin, dtype, tol, T, wi
         _close(got, ref, tol)
     gu = (torch.randn(T, 2 * inter, generator=g) * 3).to(DEV, dtype)
     _close(kernels.glu_clamped(gu, 1.5, 1.702), twin._glu_clamped(gu, 1.5, 1.702).to(dtype), tol)
+
+
+def test_router_with_more_choices_than_a_warp_has_lanes(kernels, twin):
+    g = torch.Generator().manual_seed(8)
+    x = torch.randn(5, 48, generator=g).to(DEV)
+    w = torch.randn(70, 48, generator=g).to(DEV)
+    choice, weight, _ = kernels.route_top(x, w, 70, 40, False)
+    c_ref, w_ref, _ = twin.route_top(x, w, 70, 40, False)
+    assert torch.equal(choice, c_ref)
+    _close(weight, w_ref, 1e-5)
 
 
 def test_equal_router_logits_go_to_the_lower_index(kernels):

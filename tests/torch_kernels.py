@@ -194,6 +194,10 @@ class TorchKernels:
             start += n
         return out.to(q_latent.dtype)
 
+    def latent_attention_out(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, w_uv, gate):
+        mixed = self.latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim)
+        return self.gate_heads(self.heads_linear(mixed, w_uv), gate)
+
     def gate_heads(self, out, gate):
         T, H, V = out.shape
         o = out.float()

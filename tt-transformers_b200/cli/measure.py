@@ -545,7 +545,7 @@ class KernelTimer:
         return out                                     # microseconds per name
 
 
-_TIMED = {"Bozavik": ["add_layernorm", "latent_prepare", "heads_linear", "latent_attention", "gate_heads", "route_top",
+_TIMED = {"Bozavik": ["add_layernorm", "latent_prepare", "heads_linear", "_latent_attention", "latent_out", "gate_heads", "route_top",
                       "routed_experts", "linear_glu_clamped", "linear"],
           "Llama": ["add_rmsnorm", "rope_kv_write", "fused_qkv_rope", "paged_attention", "linear_swiglu", "linear"]}
 
@@ -665,6 +665,7 @@ def run_design_comparison(name: str = "bozavik-a", *, prefill_tokens: int = PREF
 def _roofline_rows(times: Dict[str, float], work: Dict[str, dict], pk: dict) -> Dict[str, dict]:
     rows = {}
     for name, us in sorted(times.items()):
+        name = name.lstrip("_")
         row = {"us": round(us, 1)}
         w = work.get(name)
         if w and us > 0:

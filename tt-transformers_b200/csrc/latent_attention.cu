@@ -15,7 +15,7 @@
 #define LA_TILE 128
 #define LA_THREADS 128
 #define LA_HEADS 8
-#define LA_MAX_ACC 4   // latent <= LA_MAX_ACC * LA_THREADS
+#define LA_MAX_ACC 4   // output columns per block: LA_MAX_ACC * LA_THREADS
 
 // ---------------------------------------------------------------- latent_prepare
 template <typename TO>
@@ -109,6 +109,7 @@ latent_attention_generic_kernel(const T* __restrict__ q_lat, long long ql_stride
     pdl_launch_dependents();
     const int t = blockIdx.x, h0 = blockIdx.y * LA_HEADS;
     const int nh = min(LA_HEADS, heads - h0);
+    const int col_base = blockIdx.z * LA_MAX_ACC * LA_THREADS;      // this block's share of the output columns
     const int pos = positions[t];
     const int lo = (window > 0 && pos - window + 1 > 0) ? pos - window + 1 : 0;
     const int* table = block_table + (size_t)seg_of_token[t] * table_width;
@@ -204,7 +205,7 @@ latent_attention_generic_kernel(const T* __restrict__ q_lat, long long ql_stride
         const int k_end = (tile * LA_TILE + LA_TILE - 1 > pos) ? pos - tile * LA_TILE + 1 : LA_TILE;
 #pragma unroll
         for (int a = 0; a < LA_MAX_ACC; ++a) {
-            const int d = threadIdx.x + a * LA_THREADS;
+            const int d = col_base + threadIdx.x + a * LA_THREADS;
             if (d < latent) {
                 float sum[LA_HEADS];
 #pragma unroll
@@ -228,7 +229,7 @@ latent_attention_generic_kernel(const T* __restrict__ q_lat, long long ql_stride
             T* dst = out + ((size_t)t * heads + h0 + h) * latent;
 #pragma unroll
             for (int a = 0; a < LA_MAX_ACC; ++a) {
-                const int d = threadIdx.x + a * LA_THREADS;
+                const int d = col_base + threadIdx.x + a * LA_THREADS;
                 if (d < latent) dst[d] = from_float<T>(acc[a][h] * inv);
             }
         }
@@ -245,14 +246,15 @@ TTB_EXPORT int ttb_latent_attention_generic(const void* q_lat, long long ql_stri
     if (tokens == 0) return TTB_OK;
     if (!q_lat || !out || !positions || !seg_of_token || !rows || !block_table || !status) return TTB_ERR_ARGUMENT;
     if (extra > 0 && (!q_rot || (rotary_dim > 0 && !inv_freq))) return TTB_ERR_ARGUMENT;
-    if (latent < 1 || latent > LA_MAX_ACC * LA_THREADS || extra < 0 || rotary_dim > extra || (rotary_dim & 1))
+    if (latent < 1 || extra < 0 || rotary_dim > extra || (rotary_dim & 1))
         return TTB_ERR_UNSUPPORTED;
     if (heads < 1 || (heads + LA_HEADS - 1) / LA_HEADS > 65535) return TTB_ERR_UNSUPPORTED;
     const int dk = latent + extra, dk_pad = (dk + 3) & ~3;
     if ((dk & 7) == 0 && !aligned16(rows)) return TTB_ERR_ARGUMENT;
     const size_t smem = (size_t)LA_HEADS * (dk_pad + LA_TILE) * sizeof(float) + LA_TILE * sizeof(size_t);
     if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
-    dim3 grid(tokens, (heads + LA_HEADS - 1) / LA_HEADS);
+    // output columns beyond LA_MAX_ACC * LA_THREADS go to further blocks (blockIdx.z), which compute the scores again
+    dim3 grid(tokens, (heads + LA_HEADS - 1) / LA_HEADS, (latent + LA_MAX_ACC * LA_THREADS - 1) / (LA_MAX_ACC * LA_THREADS));
 #define LA_LAUNCH(T)                                                                                                 \
     do {                                                                                                             \
         if (smem > 48 * 1024)                                                                                        \
@@ -302,5 +304,111 @@ TTB_EXPORT int ttb_gate_heads(const void* in, long long stride_t, long long stri
                    per_head, (float*)out, heads, vdim);
     else
         return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}
+
+// ---------------------------------------------------------------- latent_out (a handful of tokens)
+// The end of the mixer for decode steps in one kernel: the key splits' partial sums are merged (or the finished
+// weighted sum of latents is read), carried through the head's W_uv and gated:
+//   out[t, h, v] = sigmoid(gate) * sum_r W_uv[h, v, r] * c[t, h, r].
+// One block per (token, head); c is float32 in shared memory; a warp works on four rows of W_uv at a time.
+#define LO_THREADS 128
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(LO_THREADS)
+latent_out_kernel(const T* __restrict__ mixed, const float* __restrict__ partial_o, const float* __restrict__ partial_ml,
+                  int splits, const T* __restrict__ w_uv, const float* __restrict__ gate, int ld_gate, int per_head,
+                  T* __restrict__ out, int heads, int latent, int vdim) {
+    extern __shared__ __align__(16) float lo_c[];          // [latent]
+    __shared__ float wt[64];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t = blockIdx.x, h = blockIdx.y;
+    const size_t row = (size_t)t * heads + h;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (splits > 1) {
+        if (warp == 0) {
+            const float2* ml = reinterpret_cast<const float2*>(partial_ml) + row * splits;
+            const float2 a = lane < splits ? ml[lane] : make_float2(-INFINITY, 0.f);
+            const float2 b = lane + 32 < splits ? ml[lane + 32] : make_float2(-INFINITY, 0.f);
+            const float M = warp_max(fmaxf(a.x, b.x));
+            const float wa = a.x == -INFINITY ? 0.f : exp2f(a.x - M), wb = b.x == -INFINITY ? 0.f : exp2f(b.x - M);
+            wt[lane] = wa * a.y;
+            wt[lane + 32] = wb * b.y;
+            __syncwarp();
+            float denom = 0.f;
+            for (int s = 0; s < splits; ++s) denom += wt[s];        // in the order of the splits
+            const float inv = denom > 0.f ? 1.f / denom : 0.f;
+            __syncwarp();
+            wt[lane] = wa * inv;
+            wt[lane + 32] = wb * inv;
+        }
+        __syncthreads();
+        for (int c = threadIdx.x; c < latent; c += LO_THREADS) {
+            const float* src = partial_o + row * splits * latent + c;
+            float acc = 0.f;
+#pragma unroll 8
+            for (int s = 0; s < splits; ++s) acc = fmaf(wt[s], src[(size_t)s * latent], acc);
+            lo_c[c] = acc;
+        }
+    } else {
+        for (int c = threadIdx.x; c < latent; c += LO_THREADS) lo_c[c] = to_float(mixed[row * latent + c]);
+    }
+    __syncthreads();
+    const T* W = w_uv + (size_t)h * vdim * latent;
+    for (int v0 = warp * 4; v0 < vdim; v0 += (LO_THREADS / 32) * 4) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        const T* rows[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) rows[i] = W + (size_t)min(v0 + i, vdim - 1) * latent;
+        if (VEC) {
+#pragma unroll 2
+            for (int k = lane * 8; k < latent; k += 256) {
+                float w[4][8];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) load8(rows[i] + k, w[i]);
+                const float4 xa = *reinterpret_cast<const float4*>(lo_c + k), xb = *reinterpret_cast<const float4*>(lo_c + k + 4);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    d[i] += w[i][0] * xa.x + w[i][1] * xa.y + w[i][2] * xa.z + w[i][3] * xa.w + w[i][4] * xb.x + w[i][5] * xb.y +
+                            w[i][6] * xb.z + w[i][7] * xb.w;
+            }
+        } else {
+            for (int k = lane; k < latent; k += 32) {
+                const float x = lo_c[k];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) d[i] = fmaf(to_float(rows[i][k]), x, d[i]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d[i] = warp_sum(d[i]);
+        if (lane < 4 && v0 + lane < vdim) {
+            float y = lane == 0 ? d[0] : lane == 1 ? d[1] : lane == 2 ? d[2] : d[3];
+            const int v = v0 + lane;
+            if (gate != nullptr) y *= 1.f / (1.f + expf(-gate[(size_t)t * ld_gate + (per_head ? h : h * vdim + v)]));
+            out[row * vdim + v] = from_float<T>(y);
+        }
+    }
+}
+
+// mixed: [tokens, heads, latent] (splits == 1) or null with partial_o / partial_ml as the attention kernel's key
+// splits left them (2 <= splits <= 64); w_uv: [heads, vdim, latent]; out: [tokens, heads * vdim].
+TTB_EXPORT int ttb_latent_out(const void* mixed, const float* partial_o, const float* partial_ml, int splits, const void* w_uv,
+                              const float* gate, int ld_gate, int per_head, void* out, int dtype, int tokens, int heads,
+                              int latent, int vdim, cudaStream_t stream) {
+    if (tokens == 0) return TTB_OK;
+    if (!w_uv || !out || splits < 1 || splits > 64) return TTB_ERR_ARGUMENT;
+    if (splits == 1 ? !mixed : (!partial_o || !partial_ml)) return TTB_ERR_ARGUMENT;
+    if (heads > 65535 || (size_t)latent * 4 > 48 * 1024) return TTB_ERR_UNSUPPORTED;
+    const bool vec = (latent & 7) == 0 && aligned16(w_uv);
+    dim3 grid(tokens, heads);
+    const size_t smem = (size_t)latent * sizeof(float);
+#define LO_LAUNCH(T, VEC)                                                                                            \
+    ttb_launch(latent_out_kernel<T, VEC>, grid, LO_THREADS, smem, stream, (const T*)mixed, partial_o, partial_ml, splits,  \
+               (const T*)w_uv, gate, ld_gate, per_head, (T*)out, heads, latent, vdim)
+    if (dtype == TTB_DTYPE_BF16) { if (vec) LO_LAUNCH(__nv_bfloat16, true); else LO_LAUNCH(__nv_bfloat16, false); }
+    else if (dtype == TTB_DTYPE_F32) { if (vec) LO_LAUNCH(float, true); else LO_LAUNCH(float, false); }
+    else return TTB_ERR_UNSUPPORTED;
+#undef LO_LAUNCH
     return ttb_launch_status();
 }

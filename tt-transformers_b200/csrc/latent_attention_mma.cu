@@ -382,8 +382,8 @@ TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t
                                         const int* seg_pos0, const void* rows, const int* block_table, int table_width,
                                         int page_size, int num_pages, int segments, int max_seg_len, int tokens, int heads,
                                         int latent, int extra, float scale, const float* sinks, const float* inv_freq,
-                                        int rotary_dim, int splits, float* partial_o, float* partial_ml, int* status,
-                                        cudaStream_t stream) {
+                                        int rotary_dim, int splits, float* partial_o, float* partial_ml, int merge,
+                                        int* status, cudaStream_t stream) {
     if (tokens == 0 || segments == 0) return TTB_OK;
     if (!q_lat || !out || !cu_seqlens || !seg_pos0 || !rows || !block_table || !status) return TTB_ERR_ARGUMENT;
     if (!ttb_latent_attention_mma_supports(latent, extra, rotary_dim, 0) || !(scale > 0.f)) return TTB_ERR_UNSUPPORTED;
@@ -419,7 +419,7 @@ TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t
     }
     ttb_launch(latent_attention_mma_kernel, dim3((unsigned)blocks_x, groups * a.chunks, splits), LM_THREADS, smem, stream, a);
     int rc = ttb_launch_status();
-    if (rc != TTB_OK || splits == 1) return rc;
+    if (rc != TTB_OK || splits == 1 || !merge) return rc;      // merge 0: the caller's next kernel takes the partial sums
     ttb_launch(latent_attention_merge_kernel, tokens * heads, 128, 0, stream, (const float*)partial_o,
                (const float*)partial_ml, (__nv_bfloat16*)out, splits, latent);
     return ttb_launch_status();

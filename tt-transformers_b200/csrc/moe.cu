@@ -53,7 +53,7 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
     // one warp picks: in round j every lane looks at its share of the experts that are still free, the lanes
     // agree on the largest logit and, among equals, on the lowest index
     if (warp == 0) {
-        float best_first = 0.f, denom = 0.f, mine = 0.f;
+        float best_first = 0.f, denom = 0.f;
         for (int j = 0; j < top; ++j) {
             float best_z = -INFINITY;
             int best = 0x7fffffff;
@@ -72,15 +72,12 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
             if (j == 0) best_first = best_z;
             const float p = expf(best_z - best_first);
             denom += p;
-            if (lane == j % 32) mine = p;                  // lane j keeps choice j's weight (top <= 32 per pass)
-            if (lane == 0) choice[(size_t)t * top + j] = best;
-            if ((j % 32 == 31 || j == top - 1)) {
-                // weights of this pass are normalised after the last round; park them unnormalised
-                const int base = j - j % 32;
-                if (base + lane <= j) weight[(size_t)t * top + base + lane] = mine;
+            if (lane == 0) {
+                choice[(size_t)t * top + j] = best;
+                weight[(size_t)t * top + j] = p;           // divided by the sum below
             }
         }
-        __syncwarp();
+        __syncwarp();                                      // lane 0's weights are visible to the warp
         for (int j = lane; j < top; j += 32) weight[(size_t)t * top + j] /= denom;
         if (shared && lane == 0) shared_gate[t] = 1.f / (1.f + expf(-z[experts]));
     }

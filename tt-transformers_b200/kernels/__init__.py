@@ -96,7 +96,7 @@ class CudaKernels:
                      "ttb_gemv_ring", "ttb_gemm_skinny_tcgen05_qkv_rope", "ttb_add_layernorm", "ttb_latent_prepare",
                      "ttb_latent_attention_generic", "ttb_gate_heads", "ttb_gemm_simt_batched", "ttb_route_top",
                      "ttb_moe_align", "ttb_moe_group_gemm", "ttb_moe_combine", "ttb_glu_clamped",
-                     "ttb_latent_attention_mma", "ttb_latent_attention_mma_supports", "ttb_moe_gemv", "ttb_moe_gemm_tcgen05",
+                     "ttb_latent_attention_mma", "ttb_latent_attention_mma_supports", "ttb_moe_gemv", "ttb_moe_gemm_tcgen05", "ttb_latent_out",
                      "ttb_latent_attention_mma_tokens_per_tile"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
@@ -647,9 +647,47 @@ class CudaKernels:
             "heads_linear")
         return out
 
+    LATENT_OUT_ROWS = 64         # up to this many tokens the end of the mixer (merge, W_uv, gate) is one kernel
+
     def latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim):
         """q_latent [T, H, latent], q_rot [T, H, extra] or None (rotated here by the tokens' positions); the cache
         rows hold [latent | extra] per token. Returns the weighted sums of the latents [T, H, latent]."""
+        return self._latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, True)[0]
+
+    def latent_attention_out(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, w_uv, gate):
+        """Attention over the latents, then per head W_uv [H, vdim, latent] and the gate (float32 logits [T, H] or
+        [T, H * vdim], or None) -> [T, H * vdim]. For a handful of tokens the key splits' merge, the per-head
+        product and the gate are one kernel."""
+        T, H, R = q_latent.shape
+        V = w_uv.shape[1]
+        if T > self.LATENT_OUT_ROWS or R * 4 > 48 * 1024:
+            mixed = self.latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim)
+            return self.gate_heads(self.heads_linear(mixed, w_uv), gate)
+        mixed, partial_o, partial_ml, splits = self._latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq,
+                                                                      rotary_dim, False)
+        return self.latent_out(mixed if splits == 1 else None, partial_o, partial_ml, splits, w_uv, gate, T, H, R)
+
+    def latent_out(self, mixed, partial_o, partial_ml, splits, w_uv, gate, T, H, R):
+        """The mixer's end for a handful of tokens in one kernel: the key splits' partial sums merged (or `mixed`
+        [T, H, latent] read), W_uv [H, vdim, latent] per head, the gate -> [T, H * vdim]."""
+        V = w_uv.shape[1]
+        if w_uv.shape != (H, V, R) or not w_uv.is_contiguous():
+            raise KernelError("latent_out: W_uv must be contiguous [heads, vdim, latent]")
+        per_head = 0
+        if gate is not None:
+            if gate.dtype != torch.float32 or gate.stride(1) != 1 or gate.shape[1] not in (H, H * V):
+                raise KernelError("latent_out: gate must be float32 [T, heads] or [T, heads * vdim]")
+            per_head = 1 if gate.shape[1] == H and V != 1 else 0
+        res = torch.empty(T, H * V, dtype=w_uv.dtype, device=self.device)
+        self._check(self.lib.ttb_latent_out(
+            self._p(mixed), self._p(partial_o), self._p(partial_ml), splits, self._p(w_uv),
+            self._p(gate), gate.stride(0) if gate is not None else 0, per_head, self._p(res), _dtype_code(res.dtype), T, H, R,
+            V, self._stream()), "latent_out")
+        return res
+
+    def _latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, merge):
+        """-> (weighted sums [T, H, latent], partial sums, their maxima and sums, number of key splits); with merge
+        False and more than one split the first is not filled in and the partial results are the caller's to merge."""
         T, H, R = q_latent.shape
         if R != view.latent or q_latent.dtype != view.rows.dtype or q_latent.stride(2) != 1:
             raise KernelError("latent_attention: the queries do not fit the cache rows")
@@ -676,10 +714,10 @@ class CudaKernels:
                 self._p(batch.seg_pos0), self._p(view.rows), self._p(view.block_table), view.block_table.shape[1],
                 view.page_size, view.rows.shape[0], batch.num_segments, batch.max_seg_len, T, H, R, view.extra,
                 ctypes.c_float(scale), self._p(sinks), self._p(inv_freq), int(rotary_dim), splits, self._p(partial_o),
-                self._p(partial_ml), self._p(self.status), self._stream()), "latent_attention_mma")
-            if splits > 1:
+                self._p(partial_ml), 1 if merge else 0, self._p(self.status), self._stream()), "latent_attention_mma")
+            if splits > 1 and merge:
                 self.launches += 1
-            return out
+            return out, partial_o, partial_ml, splits
         self._check(self.lib.ttb_latent_attention_generic(
             self._p(q_latent), ctypes.c_longlong(q_latent.stride(0)), ctypes.c_longlong(q_latent.stride(1)),
             self._p(q_rot), ctypes.c_longlong(q_rot.stride(0) if q_rot is not None else 0),
@@ -688,7 +726,7 @@ class CudaKernels:
             view.block_table.shape[1], view.page_size, T, H, R, view.extra, ctypes.c_float(scale), self._p(sinks),
             self._p(inv_freq), int(rotary_dim), int(view.window or 0), view.rows.shape[0], self._p(self.status),
             self._stream()), "latent_attention")
-        return out
+        return out, None, None, 1
 
     def gate_heads(self, out, gate):
         """out [T, H, V] (any token and head strides) times sigmoid(gate), gate float32 [T, H] or [T, H * V] or

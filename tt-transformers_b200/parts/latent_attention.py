@@ -92,11 +92,11 @@ class LatentAttention(Mixer):
                                cache, write_cache, self.runtime.dtype)
         q = k.linear(c_q, self.w_uq).view(-1, H, D + rot)
         q_latent = k.heads_linear(q[:, :, :D], self.w_uk_t)                       # [T, H, R]
-        mixed = k.latent_attention(q_latent, q[:, :, D:] if rot else None, batch, cache, self.scale, self.sinks,
-                                   inv_freq, rotary_dim)                           # [T, H, R]
-        out = k.heads_linear(mixed, self.w_uv)                                      # [T, H, vdim]
         gate = down[:, self.q_rank + R + rot:] if self.gate else None
-        return k.linear(k.gate_heads(out, gate), self.w_o)
+        # the weighted sums of the latents [T, H, R], through W_uv per head, gated: [T, H * vdim]
+        out = k.latent_attention_out(q_latent, q[:, :, D:] if rot else None, batch, cache, self.scale, self.sinks,
+                                     inv_freq, rotary_dim, self.w_uv, gate)
+        return k.linear(out, self.w_o)
 
 
 register_part("mixer", "latent_attention", LatentAttention)
