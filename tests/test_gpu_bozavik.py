@@ -219,10 +219,12 @@ def test_router_and_experts_against_their_twins(kernels, twin, dtype, tol, T, wi
     assert torch.allclose(weight.sum(-1), torch.ones(T, device=DEV), atol=1e-5)
     w_gate_up = (torch.randn(E, 2 * inter, width, generator=g) * width ** -0.5 * 3).to(DEV, dtype)   # large enough to meet the limit
     w_down = (torch.randn(E, width, inter, generator=g) * inter ** -0.5).to(DEV, dtype)
-    shared = torch.randn(T, width, generator=g).to(DEV, dtype)
-    for shared_out, shared_gate in ((shared, gate), (None, None)):
-        got = kernels.routed_experts(x, choice, weight, w_gate_up, w_down, 1.5, 1.702, shared_out, shared_gate)
-        ref = twin.routed_experts(x, choice, weight, w_gate_up, w_down, 1.5, 1.702, shared_out, shared_gate)
+    s_inter = 40
+    shared = ((torch.randn(2 * s_inter, width, generator=g) * width ** -0.5 * 3).to(DEV, dtype),
+              (torch.randn(width, s_inter, generator=g) * s_inter ** -0.5).to(DEV, dtype), 0.7)
+    for shared_expert, shared_gate in ((shared, gate), (None, None)):
+        got = kernels.routed_experts(x, choice, weight, w_gate_up, w_down, 1.5, 1.702, shared_expert, shared_gate)
+        ref = twin.routed_experts(x, choice, weight, w_gate_up, w_down, 1.5, 1.702, shared_expert, shared_gate)
         assert got.dtype == torch.float32
         _close(got, ref, tol)
     gu = (torch.randn(T, 2 * inter, generator=g) * 3).to(DEV, dtype)

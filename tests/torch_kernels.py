@@ -225,7 +225,7 @@ class TorchKernels:
     def linear_glu_clamped(self, x, w_gate_up, limit, alpha):
         return self._glu_clamped(self.linear(x, w_gate_up), limit, alpha).to(x.dtype)
 
-    def routed_experts(self, x, choice, weight, w_gate_up, w_down, limit, alpha, shared_out, shared_gate):
+    def routed_experts(self, x, choice, weight, w_gate_up, w_down, limit, alpha, shared=None, shared_gate=None):
         T, top = choice.shape
         out = torch.zeros(T, w_down.shape[1], dtype=torch.float32, device=x.device)
         for t in range(T):
@@ -233,7 +233,8 @@ class TorchKernels:
                 e = int(choice[t, j])
                 hidden = self._glu_clamped(self.linear(x[t:t + 1], w_gate_up[e]), limit, alpha).to(x.dtype)
                 out[t] += weight[t, j] * self.linear(hidden, w_down[e]).float()[0]
-        if shared_out is not None:
+        if shared is not None:
+            shared_out = self.linear(self.linear_glu_clamped(x, shared[0], shared[2], alpha), shared[1])
             out += shared_out.float() * shared_gate[:, None]
         return out
 

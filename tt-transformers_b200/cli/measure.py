@@ -546,7 +546,7 @@ class KernelTimer:
 
 
 _TIMED = {"Bozavik": ["add_layernorm", "latent_prepare", "heads_linear", "_latent_attention", "latent_out", "gate_heads", "route_top",
-                      "routed_experts", "linear_glu_clamped", "linear"],
+                      "routed_experts", "linear"],
           "Llama": ["add_rmsnorm", "rope_kv_write", "fused_qkv_rope", "paged_attention", "linear_swiglu", "linear"]}
 
 
@@ -573,7 +573,9 @@ def _kernel_work(cfg: dict, tokens: int, contexts: List[int], new_per_request: i
             if f:
                 top, ff, experts = f["router"]["top"], f["expert"]["ff"], f["router"]["experts"]
                 used = min(experts, tokens * top)
-                add("routed_experts", 2 * tokens * top * 3 * ff * width, 2 * used * 3 * ff * width + tokens * width * (2 + 4))
+                sff = (f.get("shared") or {}).get("ff", 0)          # the shared expert runs inside the same call
+                add("routed_experts", 2 * tokens * 3 * (top * ff + sff) * width,
+                    2 * (used * ff + sff) * 3 * width + tokens * width * (2 + 4))
     else:
         width, heads, kv, hd = cfg["hidden_size"], cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
         for _ in range(cfg["num_hidden_layers"]):

@@ -489,18 +489,29 @@ template <typename T, bool VEC>
 __global__ void __launch_bounds__(MV_THREADS)
 moe_gemv_first_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ W, long long w_expert_stride,
                       const int* __restrict__ choice, int experts, int top, T* __restrict__ hidden, int N, int K,
-                      float limit, float alpha) {
+                      float limit, float alpha, int pairs, const T* __restrict__ shared_w, T* __restrict__ shared_hidden,
+                      int shared_n, float shared_limit) {
     extern __shared__ __align__(16) float mv_x[];          // [K]
     pdl_wait();
     pdl_launch_dependents();
-    const int p = blockIdx.y, e = choice[p];
-    const T* row = x + (size_t)(p / top) * ldx;
+    int p = blockIdx.y, e = 0;
+    const bool is_shared = p >= pairs;                      // rows past the pairs: the shared expert of token p - pairs
+    if (is_shared) {
+        W = shared_w;
+        hidden = shared_hidden;
+        N = shared_n;
+        limit = shared_limit;
+        p -= pairs;
+    } else {
+        e = choice[p];
+    }
+    const T* row = x + (size_t)(is_shared ? p : p / top) * ldx;
     for (int k = threadIdx.x; k < K; k += MV_THREADS) mv_x[k] = to_float(row[k]);
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int n_begin = (blockIdx.x * (MV_THREADS / 32) + warp) * MV_ROWS_PER_WARP;
     if (n_begin >= N) return;
-    const bool valid = (unsigned)e < (unsigned)experts;
+    const bool valid = is_shared || (unsigned)e < (unsigned)experts;
     const T* We = W + (size_t)(valid ? e : 0) * w_expert_stride;
     const T* rows[2 * MV_ROWS_PER_WARP];
 #pragma unroll
@@ -525,12 +536,14 @@ __global__ void __launch_bounds__(MV_THREADS)
 moe_gemv_second_kernel(const T* __restrict__ hidden, const T* __restrict__ W, long long w_expert_stride,
                        const int* __restrict__ choice, const float* __restrict__ weight, int experts, int top,
                        const T* __restrict__ shared_out, const float* __restrict__ shared_gate, float* __restrict__ out,
-                       int N, int K) {
-    extern __shared__ __align__(16) float mv_h[];          // [top, K]
+                       int N, int K, const T* __restrict__ shared_w, const T* __restrict__ shared_hidden, int shared_k) {
+    extern __shared__ __align__(16) float mv_h[];          // [top, K] then [shared_k]
     pdl_wait();
     pdl_launch_dependents();
     const int t = blockIdx.y;
     for (int i = threadIdx.x; i < top * K; i += MV_THREADS) mv_h[i] = to_float(hidden[(size_t)t * top * K + i]);
+    if (shared_w != nullptr)
+        for (int i = threadIdx.x; i < shared_k; i += MV_THREADS) mv_h[top * K + i] = to_float(shared_hidden[(size_t)t * shared_k + i]);
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int n_begin = (blockIdx.x * (MV_THREADS / 32) + warp) * MV_ROWS_PER_WARP;
@@ -551,6 +564,16 @@ moe_gemv_second_kernel(const T* __restrict__ hidden, const T* __restrict__ W, lo
 #pragma unroll
         for (int i = 0; i < MV_ROWS_PER_WARP; ++i) acc[i] = fmaf(wj, d[i], acc[i]);
     }
+    if (shared_w != nullptr) {                  // the shared expert's down product, times the token's gate
+        const T* rows[MV_ROWS_PER_WARP];
+#pragma unroll
+        for (int i = 0; i < MV_ROWS_PER_WARP; ++i) rows[i] = shared_w + (size_t)min(n_begin + i, N - 1) * shared_k;
+        float d[MV_ROWS_PER_WARP];
+        mv_dots<T, VEC, MV_ROWS_PER_WARP>(rows, mv_h + (size_t)top * K, shared_k, lane, d);
+        const float sg = shared_gate[t];
+#pragma unroll
+        for (int i = 0; i < MV_ROWS_PER_WARP; ++i) acc[i] = fmaf(sg, d[i], acc[i]);
+    }
     if (lane < MV_ROWS_PER_WARP && n_begin + lane < N) {
         float v = 0.f;
 #pragma unroll
@@ -563,28 +586,38 @@ moe_gemv_second_kernel(const T* __restrict__ hidden, const T* __restrict__ W, lo
 }
 
 // x [tokens, width]; w_gate_up [experts, 2 inter, width]; w_down [experts, width, inter]; hidden: scratch
-// [tokens * top, inter] of the compute type; out float32 [tokens, width]; shared_out of the compute type or null.
+// [tokens * top, inter] of the compute type; out float32 [tokens, width]. The shared expert either comes as its
+// finished output (shared_out, compute type) or as its weights (shared_gate_up [2 shared_inter, width], shared_down
+// [width, shared_inter], scratch shared_hidden [tokens, shared_inter]) and then runs inside the two kernels; or not at all.
 TTB_EXPORT int ttb_moe_gemv(const void* x, int ldx, const void* w_gate_up, const void* w_down, const int* choice,
                             const float* weight, void* hidden, const void* shared_out, const float* shared_gate, float* out,
                             int dtype, int tokens, int experts, int top, int inter, int width, float limit, float alpha,
-                            cudaStream_t stream) {
+                            const void* shared_gate_up, const void* shared_down, void* shared_hidden, int shared_inter,
+                            float shared_limit, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
-    if (!x || !w_gate_up || !w_down || !choice || !weight || !hidden || !out || (shared_out && !shared_gate)) return TTB_ERR_ARGUMENT;
+    if (!x || !w_gate_up || !w_down || !choice || !weight || !hidden || !out) return TTB_ERR_ARGUMENT;
+    if ((shared_out || shared_gate_up) && !shared_gate) return TTB_ERR_ARGUMENT;
+    if (shared_gate_up && (!shared_down || !shared_hidden || shared_inter < 1 || shared_out)) return TTB_ERR_ARGUMENT;
     const int pairs = tokens * top;
-    if (pairs > 65535) return TTB_ERR_UNSUPPORTED;
-    const size_t smem1 = (size_t)width * sizeof(float), smem2 = (size_t)top * inter * sizeof(float);
+    const int sk = shared_gate_up ? shared_inter : 0;
+    if (pairs + tokens > 65535) return TTB_ERR_UNSUPPORTED;
+    const size_t smem1 = (size_t)width * sizeof(float), smem2 = ((size_t)top * inter + sk) * sizeof(float);
     if (smem1 > 48 * 1024 || smem2 > 48 * 1024) return TTB_ERR_UNSUPPORTED;
     const int per_block = (MV_THREADS / 32) * MV_ROWS_PER_WARP;
-    dim3 g1((inter + per_block - 1) / per_block, pairs), g2((width + per_block - 1) / per_block, tokens);
+    const int widest = inter > sk ? inter : sk;
+    dim3 g1((widest + per_block - 1) / per_block, pairs + (shared_gate_up ? tokens : 0)), g2((width + per_block - 1) / per_block, tokens);
     const long long s1 = 2LL * inter * width, s2 = (long long)width * inter;
 #define MV_LAUNCH(T, VEC)                                                                                            \
     do {                                                                                                             \
         ttb_launch(moe_gemv_first_kernel<T, VEC>, g1, MV_THREADS, smem1, stream, (const T*)x, ldx, (const T*)w_gate_up, s1, \
-                   choice, experts, top, (T*)hidden, inter, width, limit, alpha);                                    \
+                   choice, experts, top, (T*)hidden, inter, width, limit, alpha, pairs, (const T*)shared_gate_up,    \
+                   (T*)shared_hidden, sk, shared_limit);                                                             \
         ttb_launch(moe_gemv_second_kernel<T, VEC>, g2, MV_THREADS, smem2, stream, (const T*)hidden, (const T*)w_down, s2,  \
-                   choice, weight, experts, top, (const T*)shared_out, shared_gate, out, width, inter);              \
+                   choice, weight, experts, top, (const T*)shared_out, shared_gate, out, width, inter,               \
+                   (const T*)(shared_gate_up ? shared_down : nullptr), (const T*)shared_hidden, sk);                 \
     } while (0)
-    const bool vec = (width & 7) == 0 && (inter & 7) == 0 && aligned32(w_gate_up) && aligned32(w_down);
+    const bool vec = (width & 7) == 0 && (inter & 7) == 0 && (sk & 7) == 0 && aligned32(w_gate_up) && aligned32(w_down) &&
+                     (!shared_gate_up || (aligned32(shared_gate_up) && aligned32(shared_down)));
     if (dtype == TTB_DTYPE_BF16) { if (vec) MV_LAUNCH(__nv_bfloat16, true); else MV_LAUNCH(__nv_bfloat16, false); }
     else if (dtype == TTB_DTYPE_F32) { if (vec) MV_LAUNCH(float, true); else MV_LAUNCH(float, false); }
     else return TTB_ERR_UNSUPPORTED;

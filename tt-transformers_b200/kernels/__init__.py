@@ -776,27 +776,37 @@ class CudaKernels:
         w_gate_up = [Wg; Wu] stacked along the rows."""
         return self.glu_clamped(self.linear(x, w_gate_up), limit, alpha)
 
-    def routed_experts(self, x, choice, weight, w_gate_up, w_down, limit, alpha, shared_out, shared_gate):
+    def routed_experts(self, x, choice, weight, w_gate_up, w_down, limit, alpha, shared=None, shared_gate=None):
         """x [T, width]; choice, weight [T, top]; w_gate_up [E, 2 inter, width]; w_down [E, width, inter] ->
-        float32 [T, width]: sum_j weight[t, j] * expert_choice[t, j](x[t]) (+ shared_gate[t] * shared_out[t])."""
+        float32 [T, width]: sum_j weight[t, j] * expert_choice[t, j](x[t]) + shared_gate[t] * shared_expert(x[t]).
+        shared: None or (w_gate_up [2 s, width], w_down [width, s], limit) of the expert every token uses."""
         T, width = x.shape
         E, two_inter, _ = w_gate_up.shape
         inter, top = two_inter // 2, choice.shape[1]
         pairs = T * top
         if x.dtype != w_gate_up.dtype or x.stride(1) != 1 or not w_gate_up.is_contiguous() or not w_down.is_contiguous():
             raise KernelError("routed_experts: operands must share a dtype and be contiguous")
-        if shared_out is not None and (shared_out.shape != (T, width) or not shared_out.is_contiguous()):
-            raise KernelError("routed_experts: the shared expert's output must be contiguous [T, width]")
+        if shared is not None and (shared_gate is None or not shared[0].is_contiguous() or not shared[1].is_contiguous()):
+            raise KernelError("routed_experts: the shared expert needs contiguous weights and a gate per token")
         out = torch.empty(T, width, dtype=torch.float32, device=self.device)
         hidden = torch.empty(pairs, inter, dtype=x.dtype, device=self.device)
-        if pairs <= self.MOE_GEMV_PAIRS and width * 4 <= 48 * 1024 and top * inter * 4 <= 48 * 1024:
-            # a handful of pairs (decode): every pair streams its expert's rows, no grouping
+        shared_inter = shared[0].shape[0] // 2 if shared is not None else 0
+        if pairs <= self.MOE_GEMV_PAIRS and width * 4 <= 48 * 1024 and (top * inter + shared_inter) * 4 <= 48 * 1024:
+            # a handful of pairs (decode): every pair streams its expert's rows, no grouping; the shared expert runs
+            # inside the same two kernels as one more expert per token
+            shared_hidden = torch.empty(T, shared_inter, dtype=x.dtype, device=self.device) if shared is not None else None
             self._check(self.lib.ttb_moe_gemv(
                 self._p(x), x.stride(0), self._p(w_gate_up), self._p(w_down), self._p(choice), self._p(weight),
-                self._p(hidden), self._p(shared_out), self._p(shared_gate), self._p(out), _dtype_code(x.dtype), T, E, top,
-                inter, width, ctypes.c_float(limit), ctypes.c_float(alpha), self._stream()), "moe_gemv")
+                self._p(hidden), None, self._p(shared_gate), self._p(out), _dtype_code(x.dtype), T, E, top,
+                inter, width, ctypes.c_float(limit), ctypes.c_float(alpha),
+                self._p(shared[0] if shared is not None else None), self._p(shared[1] if shared is not None else None),
+                self._p(shared_hidden), shared_inter, ctypes.c_float(shared[2] if shared is not None else 0.0),
+                self._stream()), "moe_gemv")
             self.launches += 1
             return out
+        shared_out = None
+        if shared is not None:
+            shared_out = self.linear(self.linear_glu_clamped(x, shared[0], shared[2], alpha), shared[1])
         offsets = torch.empty(E + 1, dtype=torch.int32, device=self.device)
         order = torch.empty(pairs, dtype=torch.int32, device=self.device)
         code = _dtype_code(x.dtype)

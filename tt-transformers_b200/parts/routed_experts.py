@@ -64,12 +64,9 @@ class RoutedExperts(FeedForward):
         k = self.runtime.kernels
         shared = self.shared_inter is not None
         choice, weight, shared_gate = k.route_top(x, self.w_router, self.experts, self.top, shared)
-        shared_out = None
-        if shared:
-            hidden = k.linear_glu_clamped(x, self.ws_gate_up, self.shared_limit, self.alpha)
-            shared_out = k.linear(hidden, self.ws_down)
+        shared_expert = (self.ws_gate_up, self.ws_down, self.shared_limit) if shared else None
         return k.routed_experts(x, choice, weight, self.w_gate_up, self.w_down, self.limit, self.alpha,
-                                shared_out, shared_gate)       # float32 [T, width]
+                                shared_expert, shared_gate)       # float32 [T, width]
 
 
 register_part("feed_forward", "routed_experts", RoutedExperts)
