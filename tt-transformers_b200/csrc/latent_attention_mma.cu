@@ -19,7 +19,8 @@
 #define LM_ROWS 64
 #define LM_KEYS 64
 #define LM_THREADS 128
-#define LM_CHUNK 128
+#define LM_CHUNK_SMALL 128     // output columns per block: one chunk holds latents up to 128 columns,
+#define LM_CHUNK_LARGE 256     // or up to 256 (more registers, fewer blocks an SM); wider latents take several chunks
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
     const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
@@ -78,6 +79,7 @@ struct LatentMmaArgs {
 };
 
 // One query tile of one segment against its share of the key tiles.
+template <int LM_CHUNK>
 __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, int seg, int tile_in_seg) {
     extern __shared__ __align__(16) unsigned char lm_smem[];
     const int dk = a.latent + a.extra, ldq = dk + 8, vecs = dk / 8;
@@ -306,15 +308,16 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
 
 // A block takes a query tile from the end of its segment (many keys) and then its partner from the start (few), so
 // that all blocks of a long prompt portion walk about the same number of key tiles.
+template <int LM_CHUNK>
 __global__ void __launch_bounds__(LM_THREADS)
 latent_attention_mma_kernel(const LatentMmaArgs a) {
     pdl_wait();
     const int seg = blockIdx.x % a.segments, b = blockIdx.x / a.segments;
     const int first = a.tiles_per_seg - 1 - b, second = a.paired ? b : first;
-    latent_attention_tile(a, seg, first);
+    latent_attention_tile<LM_CHUNK>(a, seg, first);
     if (second != first) {
         __syncthreads();                      // the first tile's queries are no longer read
-        latent_attention_tile(a, seg, second);
+        latent_attention_tile<LM_CHUNK>(a, seg, second);
     }
     pdl_launch_dependents();
 }
@@ -399,7 +402,8 @@ TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t
     a.heads_per_group = heads < LM_ROWS ? heads : LM_ROWS;
     a.tokens_per_tile = ttb_latent_attention_mma_tokens_per_tile(heads);
     a.tiles_per_seg = (max_seg_len + a.tokens_per_tile - 1) / a.tokens_per_tile;
-    a.chunks = (latent + LM_CHUNK - 1) / LM_CHUNK;
+    const int chunk_cols = latent > LM_CHUNK_SMALL ? LM_CHUNK_LARGE : LM_CHUNK_SMALL;
+    a.chunks = (latent + chunk_cols - 1) / chunk_cols;
     a.segments = segments;
     a.latent = latent; a.extra = extra; a.rotary_dim = rotary_dim;
     a.scale_log2 = scale * 1.4426950408889634f; a.sinks = sinks; a.inv_freq = inv_freq;
@@ -414,10 +418,14 @@ TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t
     const size_t smem = (size_t)(1 + a.stages) * tile_bytes;
     static TtbOncePerDevice once;
     if (once.pending()) {
-        cudaFuncSetAttribute(latent_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        cudaFuncSetAttribute(latent_attention_mma_kernel<LM_CHUNK_SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        cudaFuncSetAttribute(latent_attention_mma_kernel<LM_CHUNK_LARGE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
         once.mark();
     }
-    ttb_launch(latent_attention_mma_kernel, dim3((unsigned)blocks_x, groups * a.chunks, splits), LM_THREADS, smem, stream, a);
+    if (chunk_cols == LM_CHUNK_SMALL)
+        ttb_launch(latent_attention_mma_kernel<LM_CHUNK_SMALL>, dim3((unsigned)blocks_x, groups * a.chunks, splits), LM_THREADS, smem, stream, a);
+    else
+        ttb_launch(latent_attention_mma_kernel<LM_CHUNK_LARGE>, dim3((unsigned)blocks_x, groups * a.chunks, splits), LM_THREADS, smem, stream, a);
     int rc = ttb_launch_status();
     if (rc != TTB_OK || splits == 1 || !merge) return rc;      // merge 0: the caller's next kernel takes the partial sums
     ttb_launch(latent_attention_merge_kernel, tokens * heads, 128, 0, stream, (const float*)partial_o,

@@ -699,7 +699,7 @@ class CudaKernels:
                 and self.lib.ttb_latent_attention_mma_supports(R, view.extra, int(rotary_dim), int(view.window or 0))):
             # tensor cores; few blocks (decode): the keys are split over blocks and merged afterwards
             per_tile = int(self.lib.ttb_latent_attention_mma_tokens_per_tile(H))
-            blocks = batch.num_segments * -(-batch.max_seg_len // per_tile) * -(-H // 64) * -(-R // 128)
+            blocks = batch.num_segments * -(-batch.max_seg_len // per_tile) * -(-H // 64) * -(-R // (256 if R > 128 else 128))
             splits = 1
             if blocks < self.sm_count:
                 splits = max(1, min(-(-2 * self.sm_count // blocks), batch.max_context // 128, 64))
