@@ -18,50 +18,57 @@
 #define LA_MAX_ACC 4   // output columns per block: LA_MAX_ACC * LA_THREADS
 
 // ---------------------------------------------------------------- latent_prepare
+// A warp per token (eight tokens a block): both sums of squares are warp reductions, nothing waits on the block.
+#define LP_WARPS 8
 template <typename TO>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(LP_WARPS * 32)
 latent_prepare_kernel(const float* __restrict__ down, int ld_down, int q_rank, int kv_rank, int rot_dim,
                       const float* __restrict__ q_norm, const float* __restrict__ kv_norm, float eps,
                       const float* __restrict__ inv_freq, int rotary_dim, const int* __restrict__ positions,
                       const int* __restrict__ seg_of_token, TO* __restrict__ cq, TO* __restrict__ rows,
                       const int* __restrict__ block_table, int table_width, int page_size, int num_pages, int write,
-                      int* __restrict__ status) {
-    __shared__ float scratch[32];
+                      int tokens, int* __restrict__ status) {
     pdl_wait();
     pdl_launch_dependents();
-    const int t = blockIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * LP_WARPS + (threadIdx.x >> 5);
+    if (t >= tokens) return;
     const float* src = down + (size_t)t * ld_down;
-    float s = 0.f;
-    for (int c = threadIdx.x; c < q_rank; c += blockDim.x) s += src[c] * src[c];
-    const float q_scale = rsqrtf(block_sum(s, scratch) / (float)q_rank + eps);
-    for (int c = threadIdx.x; c < q_rank; c += blockDim.x) cq[(size_t)t * q_rank + c] = from_float<TO>(src[c] * q_scale * q_norm[c]);
-    if (!write) return;
-    const int pos = positions[t];
-    const int page_index = pos / page_size;
-    int page = -1;
-    if (page_index < table_width) page = block_table[(size_t)seg_of_token[t] * table_width + page_index];
-    else if (threadIdx.x == 0) atomicExch(status, 0x1000000 + t);       // a position beyond the block table
-    if (page_index < table_width && (unsigned)page >= (unsigned)num_pages) {
-        if (threadIdx.x == 0) atomicExch(status, 0x2000000 + t);         // a page id outside the pool
-        page = -1;
-    }
     const float* c_src = src + q_rank;
-    s = 0.f;
-    for (int c = threadIdx.x; c < kv_rank; c += blockDim.x) s += c_src[c] * c_src[c];
-    const float c_scale = rsqrtf(block_sum(s, scratch) / (float)kv_rank + eps);
+    // where the token's row goes (looked up while the sums are formed)
+    int pos = 0, page = -1;
+    if (write) {
+        pos = positions[t];
+        const int page_index = pos / page_size;
+        if (page_index < table_width) {
+            page = block_table[(size_t)seg_of_token[t] * table_width + page_index];
+            if ((unsigned)page >= (unsigned)num_pages) {
+                if (lane == 0) atomicExch(status, 0x2000000 + t);         // a page id outside the pool
+                page = -1;
+            }
+        } else if (lane == 0) {
+            atomicExch(status, 0x1000000 + t);                             // a position beyond the block table
+        }
+    }
+    float sq = 0.f, sc = 0.f;
+    for (int c = lane; c < q_rank; c += 32) sq = fmaf(src[c], src[c], sq);
+    for (int c = lane; c < kv_rank; c += 32) sc = fmaf(c_src[c], c_src[c], sc);
+    const float q_scale = rsqrtf(warp_sum(sq) / (float)q_rank + eps);
+    const float c_scale = rsqrtf(warp_sum(sc) / (float)kv_rank + eps);
+    for (int c = lane; c < q_rank; c += 32) cq[(size_t)t * q_rank + c] = from_float<TO>(src[c] * q_scale * q_norm[c]);
     if (page < 0) return;
     TO* dst = rows + ((size_t)page * page_size + (pos % page_size)) * (kv_rank + rot_dim);
-    for (int c = threadIdx.x; c < kv_rank; c += blockDim.x) dst[c] = from_float<TO>(c_src[c] * c_scale * kv_norm[c]);
+    for (int c = lane; c < kv_rank; c += 32) dst[c] = from_float<TO>(c_src[c] * c_scale * kv_norm[c]);
     const float* r_src = c_src + kv_rank;
     const int half = rotary_dim / 2;
-    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    for (int i = lane; i < half; i += 32) {
         float sn, cs;
         sincosf((float)pos * inv_freq[i], &sn, &cs);
         const float u = r_src[i], v = r_src[i + half];
         dst[kv_rank + i] = from_float<TO>(u * cs - v * sn);
         dst[kv_rank + i + half] = from_float<TO>(v * cs + u * sn);
     }
-    for (int i = rotary_dim + threadIdx.x; i < rot_dim; i += blockDim.x) dst[kv_rank + i] = from_float<TO>(r_src[i]);
+    for (int i = rotary_dim + lane; i < rot_dim; i += 32) dst[kv_rank + i] = from_float<TO>(r_src[i]);
 }
 
 TTB_EXPORT int ttb_latent_prepare(const float* down, int ld_down, int q_rank, int kv_rank, int rot_dim,
@@ -74,14 +81,15 @@ TTB_EXPORT int ttb_latent_prepare(const float* down, int ld_down, int q_rank, in
     if (write && (!rows || !block_table)) return TTB_ERR_ARGUMENT;
     if (rot_dim < 0 || rotary_dim < 0 || rotary_dim > rot_dim || (rotary_dim & 1) || (rotary_dim > 0 && !inv_freq))
         return TTB_ERR_ARGUMENT;
+    const int blocks = (tokens + LP_WARPS - 1) / LP_WARPS;
     if (dtype == TTB_DTYPE_BF16)
-        ttb_launch(latent_prepare_kernel<__nv_bfloat16>, tokens, 256, 0, stream, down, ld_down, q_rank, kv_rank, rot_dim,
+        ttb_launch(latent_prepare_kernel<__nv_bfloat16>, blocks, LP_WARPS * 32, 0, stream, down, ld_down, q_rank, kv_rank, rot_dim,
                    q_norm, kv_norm, eps, inv_freq, rotary_dim, positions, seg_of_token, (__nv_bfloat16*)cq,
-                   (__nv_bfloat16*)rows, block_table, table_width, page_size, num_pages, write, status);
+                   (__nv_bfloat16*)rows, block_table, table_width, page_size, num_pages, write, tokens, status);
     else if (dtype == TTB_DTYPE_F32)
-        ttb_launch(latent_prepare_kernel<float>, tokens, 256, 0, stream, down, ld_down, q_rank, kv_rank, rot_dim, q_norm,
+        ttb_launch(latent_prepare_kernel<float>, blocks, LP_WARPS * 32, 0, stream, down, ld_down, q_rank, kv_rank, rot_dim, q_norm,
                    kv_norm, eps, inv_freq, rotary_dim, positions, seg_of_token, (float*)cq, (float*)rows, block_table,
-                   table_width, page_size, num_pages, write, status);
+                   table_width, page_size, num_pages, write, tokens, status);
     else
         return TTB_ERR_UNSUPPORTED;
     return ttb_launch_status();

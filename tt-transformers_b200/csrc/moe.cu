@@ -17,49 +17,70 @@
 #define RT_THREADS 128
 #define RT_MAX_EXPERTS 1024
 
-template <typename T>
-__global__ void __launch_bounds__(1024)
+// TPB tokens a block: a row of W_r is read once for all of them (with many tokens the reads of W_r from L2 are
+// what the kernel waits for). A warp per logit row; then a warp per token selects.
+template <typename T, int TPB>
+__global__ void __launch_bounds__(TPB == 1 ? 1024 : 512)
 route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_router, int width, int experts, int top,
-                 int shared, int* __restrict__ choice, float* __restrict__ weight, float* __restrict__ shared_gate) {
+                 int shared, int* __restrict__ choice, float* __restrict__ weight, float* __restrict__ shared_gate,
+                 int tokens) {
     extern __shared__ __align__(16) float rt_smem[];
-    float* h = rt_smem;                   // [width]
-    float* z = rt_smem + ((width + 3) & ~3);           // [experts + 1]
-    int* taken = reinterpret_cast<int*>(z + experts + 1);    // [experts]
+    const int wpad = (width + 3) & ~3;
+    float* h = rt_smem;                                   // [TPB, wpad]
+    float* z = h + TPB * wpad;                            // [TPB, experts + 1]
+    int* taken = reinterpret_cast<int*>(z + TPB * (experts + 1));    // [TPB, experts]
     pdl_wait();
     pdl_launch_dependents();
-    const int t = blockIdx.x;
-    for (int c = threadIdx.x; c < width; c += blockDim.x) h[c] = to_float(x[(size_t)t * ldx + c]);
-    for (int e = threadIdx.x; e < experts; e += blockDim.x) taken[e] = 0;
+    const int t0 = blockIdx.x * TPB, nt = min(TPB, tokens - t0);
+    for (int i = 0; i < TPB; ++i)
+        for (int c = threadIdx.x; c < wpad; c += blockDim.x)
+            h[i * wpad + c] = (i < nt && c < width) ? to_float(x[(size_t)(t0 + i) * ldx + c]) : 0.f;
+    for (int e = threadIdx.x; e < TPB * experts; e += blockDim.x) taken[e] = 0;
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const bool vec = (width & 3) == 0;
     for (int e = warp; e < experts + (shared ? 1 : 0); e += nwarps) {
         const float* w = w_router + (size_t)e * width;
-        float s = 0.f;
-        if (vec) {          // all of a lane's loads are independent: they are in flight together
-#pragma unroll 8
+        float s[TPB];
+#pragma unroll
+        for (int i = 0; i < TPB; ++i) s[i] = 0.f;
+        if (vec) {          // a lane's loads are independent of one another: they are in flight together
+#pragma unroll 4
             for (int c = lane * 4; c < width; c += 128) {
                 const float4 a = *reinterpret_cast<const float4*>(w + c);
-                const float4 b = *reinterpret_cast<const float4*>(h + c);
-                s = fmaf(a.x, b.x, s); s = fmaf(a.y, b.y, s); s = fmaf(a.z, b.z, s); s = fmaf(a.w, b.w, s);
+#pragma unroll
+                for (int i = 0; i < TPB; ++i) {
+                    const float4 b = *reinterpret_cast<const float4*>(h + i * wpad + c);
+                    s[i] = fmaf(a.x, b.x, s[i]); s[i] = fmaf(a.y, b.y, s[i]); s[i] = fmaf(a.z, b.z, s[i]); s[i] = fmaf(a.w, b.w, s[i]);
+                }
             }
         } else {
-            for (int c = lane; c < width; c += 32) s = fmaf(h[c], w[c], s);
+            for (int c = lane; c < width; c += 32) {
+                const float a = w[c];
+#pragma unroll
+                for (int i = 0; i < TPB; ++i) s[i] = fmaf(h[i * wpad + c], a, s[i]);
+            }
         }
-        s = warp_sum(s);
-        if (lane == 0) z[e] = s;
+#pragma unroll
+        for (int i = 0; i < TPB; ++i) {
+            const float r = warp_sum(s[i]);
+            if (lane == 0) z[i * (experts + 1) + e] = r;
+        }
     }
     __syncthreads();
-    // one warp picks: in round j every lane looks at its share of the experts that are still free, the lanes
-    // agree on the largest logit and, among equals, on the lowest index
-    if (warp == 0) {
+    // a warp per token picks: in round j every lane looks at its share of the experts that are still free, the
+    // lanes agree on the largest logit and, among equals, on the lowest index
+    for (int i = warp; i < nt; i += nwarps) {
+        const int t = t0 + i;
+        const float* zt = z + i * (experts + 1);
+        int* tk = taken + i * experts;
         float best_first = 0.f, denom = 0.f;
         for (int j = 0; j < top; ++j) {
             float best_z = -INFINITY;
             int best = 0x7fffffff;
             for (int e = lane; e < experts; e += 32) {
-                const float v = taken[e] ? -INFINITY : z[e];
-                if (!taken[e] && (best == 0x7fffffff || v > best_z)) { best = e; best_z = v; }
+                const float v = tk[e] ? -INFINITY : zt[e];
+                if (!tk[e] && (best == 0x7fffffff || v > best_z)) { best = e; best_z = v; }
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
@@ -67,7 +88,7 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
                 const int oe = __shfl_xor_sync(0xffffffffu, best, o);
                 if (oe != 0x7fffffff && (best == 0x7fffffff || oz > best_z || (oz == best_z && oe < best))) { best = oe; best_z = oz; }
             }
-            if (lane == 0) taken[best] = 1;
+            if (lane == 0) tk[best] = 1;
             __syncwarp();
             if (j == 0) best_first = best_z;
             const float p = expf(best_z - best_first);
@@ -79,8 +100,23 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
         }
         __syncwarp();                                      // lane 0's weights are visible to the warp
         for (int j = lane; j < top; j += 32) weight[(size_t)t * top + j] /= denom;
-        if (shared && lane == 0) shared_gate[t] = 1.f / (1.f + expf(-z[experts]));
+        if (shared && lane == 0) shared_gate[t] = 1.f / (1.f + expf(-zt[experts]));
     }
+}
+
+template <typename T, int TPB>
+static int route_top_launch(const void* x, int ldx, const float* w_router, int tokens, int width, int experts, int top,
+                            int shared, int* choice, float* weight, float* shared_gate, int threads, cudaStream_t stream) {
+    const size_t smem = ((size_t)TPB * (((width + 3) & ~3) + 2 * experts + 1)) * sizeof(float);
+    if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
+    static TtbOncePerDevice once;
+    if (smem > 48 * 1024 && once.pending()) {
+        cudaFuncSetAttribute(route_top_kernel<T, TPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        once.mark();
+    }
+    ttb_launch(route_top_kernel<T, TPB>, (tokens + TPB - 1) / TPB, threads, smem, stream, (const T*)x, ldx, w_router, width,
+               experts, top, shared, choice, weight, shared_gate, tokens);
+    return ttb_launch_status();
 }
 
 TTB_EXPORT int ttb_route_top(const void* x, int dtype, int ldx, const float* w_router, int tokens, int width, int experts,
@@ -88,22 +124,20 @@ TTB_EXPORT int ttb_route_top(const void* x, int dtype, int ldx, const float* w_r
     if (tokens == 0) return TTB_OK;
     if (!x || !w_router || !choice || !weight || (shared && !shared_gate)) return TTB_ERR_ARGUMENT;
     if (experts < 1 || experts > RT_MAX_EXPERTS || top < 1 || top > experts) return TTB_ERR_UNSUPPORTED;
-    const size_t smem = (size_t)(((width + 3) & ~3) + 2 * experts + 1) * sizeof(float);
-    if (smem > 48 * 1024) return TTB_ERR_UNSUPPORTED;
-    const int rows = experts + (shared ? 1 : 0);
-    // a warp per logit, up to 32 warps for a handful of tokens (latency) and up to 8 for many (more blocks an SM)
-    const int most = tokens > 64 ? 8 : 32;
-    const int threads = 32 * (rows < 4 ? 4 : (rows > most ? most : rows));
     if ((width & 3) == 0 && !aligned16(w_router)) return TTB_ERR_ARGUMENT;
-    if (dtype == TTB_DTYPE_BF16)
-        ttb_launch(route_top_kernel<__nv_bfloat16>, tokens, threads, smem, stream, (const __nv_bfloat16*)x, ldx, w_router,
-                   width, experts, top, shared, choice, weight, shared_gate);
-    else if (dtype == TTB_DTYPE_F32)
-        ttb_launch(route_top_kernel<float>, tokens, threads, smem, stream, (const float*)x, ldx, w_router, width, experts,
-                   top, shared, choice, weight, shared_gate);
-    else
-        return TTB_ERR_UNSUPPORTED;
-    return ttb_launch_status();
+    const int rows = experts + (shared ? 1 : 0);
+    // a handful of tokens: a block per token and a warp per logit (latency); many: eight tokens a block and up to
+    // sixteen warps (W_r is read once per block)
+    const bool many = tokens > 64 && (size_t)8 * (width + 2 * experts + 4) * sizeof(float) <= 96 * 1024;
+    const int most = many ? 16 : 32;
+    const int threads = 32 * (rows < 4 ? 4 : (rows > most ? most : rows));
+#define RT_LAUNCH(T)                                                                                                 \
+    (many ? route_top_launch<T, 8>(x, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, threads, stream) \
+          : route_top_launch<T, 1>(x, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, threads, stream))
+    if (dtype == TTB_DTYPE_BF16) return RT_LAUNCH(__nv_bfloat16);
+    if (dtype == TTB_DTYPE_F32) return RT_LAUNCH(float);
+#undef RT_LAUNCH
+    return TTB_ERR_UNSUPPORTED;
 }
 
 // ---------------------------------------------------------------- grouping
