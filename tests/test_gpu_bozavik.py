@@ -95,7 +95,7 @@ def _latent_setup(segs, H, R, extra, rotary_dim, page, dtype, seed, shuffle_page
 
 
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 2e-5), (torch.bfloat16, 2e-2)])
-@pytest.mark.parametrize("H,R,extra,rotary_dim,page", [(6, 96, 0, 0, 16), (4, 128, 32, 32, 16), (5, 40, 12, 8, 4),
+@pytest.mark.parametrize("H,R,extra,rotary_dim,page", [(7, 80, 0, 0, 16), (4, 112, 48, 32, 16), (5, 40, 12, 8, 4),
                                                        (1, 20, 0, 0, 8), (70, 32, 16, 16, 16), (3, 272, 16, 16, 32), (2, 528, 0, 0, 16)])
 def test_latent_attention_against_its_twin(kernels, twin, dtype, tol, H, R, extra, rotary_dim, page):
     # a prompt portion beside cached tokens, decoded tokens at short and long contexts, a first token, and

@@ -36,12 +36,12 @@ def bozavik_config(width, layers, heads, dim, rot_dim, vdim, q_rank, kv_rank, ex
         m = {"heads": heads, "dim": dim, "vdim": vdim, "q_rank": q_rank, "kv_rank": kv_rank,
              "scale": (dim + (rot_dim if second else 0)) ** -0.5}
         if second:
-            m.update(rot_dim=rot_dim, rot={"base": 500000.0, "dims": rot_dim})
+            m.update(rot_dim=rot_dim, rot={"base": 10000.0, "dims": rot_dim})
         return m
 
     mlp = {"kind": "moe", "router": {"experts": experts, "top": top}, "expert": {"ff": ff, "limit": 7.0},
            "shared": {"ff": shared_ff, "limit": 7.0}}
-    return {"architecture": "Bozavik", "vocab": vocab, "width": width, "residual_mult": 0.5, "norm": {"eps": 1e-6},
+    return {"architecture": "Bozavik", "vocab": vocab, "width": width, "residual_mult": 0.7, "norm": {"eps": 1e-5},
             "embedding": {"scale": 1.0},
             "layers": [{"type": "latent_attention_2" if i % 2 else "latent_attention", "mixer": mixer(i % 2 == 1),
                         "mlp": mlp} for i in range(layers)]}
