@@ -113,3 +113,25 @@ def test_the_plain_mechanisms_by_hand():
     s = 1 / (1 + np.exp(-1.702 * 2.0))
     s5 = 1 / (1 + np.exp(1.702 * 5.0))
     assert torch.allclose(y, torch.tensor([[2.0 * s * (-2.0 + 1.0), -5.0 * s5 * (2.0 + 1.0)]], dtype=torch.float32), atol=1e-5)
+
+
+def test_greedy_generation_through_the_scheduler_under_page_pressure(tmp_path):
+    from tt_transformers_b200.engine.llm import from_pretrained
+
+    folder = cases.write_folder(str(tmp_path / "g"), cases.ODD, seed=7)
+    cfg, w = cases.read_folder(folder)
+    prompts = [helpers.random_tokens(cfg["vocab"], n, 80 + n) for n in (4, 13, 21)]
+
+    def plain_greedy(prompt, new):
+        toks = list(prompt)
+        for _ in range(new):
+            toks.append(int(plain_bozavik.forward(cfg, w, toks)[-1].argmax()))
+        return toks[len(prompt):]
+
+    expect = [plain_greedy(p, 6) for p in prompts]
+    # 7 pages of 8 tokens for requests that end at 10, 19 and 27 tokens: they cannot all stay, one gives way and is recomputed
+    llm = from_pretrained(folder, dtype="float32", page_size=8, num_pages=7, max_batch_size=3, max_seq_len=64,
+                          max_step_tokens=16, max_chunk_tokens=8, device="cpu", kernels=TorchKernels())
+    assert llm.generate(prompts, max_new_tokens=6) == expect
+    llm.engine.cache.audit()
+    assert llm.engine.cache.free_pages() == 7

@@ -42,7 +42,7 @@ def _close(got, ref, tol):
 
 
 # ---------------------------------------------------------------------------- layer norm around sub-layers
-@pytest.mark.parametrize("width", [60, 128, 1000])
+@pytest.mark.parametrize("width", [60, 128, 1000, 2056])
 @pytest.mark.parametrize("delta_dtype", [None, torch.float32, torch.bfloat16])
 def test_add_layernorm(kernels, twin, width, delta_dtype):
     g = torch.Generator().manual_seed(width)

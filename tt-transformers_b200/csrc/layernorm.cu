@@ -57,6 +57,81 @@ add_layernorm_kernel(float* __restrict__ residual, const TD* __restrict__ delta,
         o[c] = from_float<TO>((row[c] - mean) * rstd * norm_w[c] + (norm_b != nullptr ? norm_b[c] : 0.f));
 }
 
+
+// Rows of up to LN_THREADS * 8 elements (a multiple of 8): a thread keeps its eight values in registers through both
+// norms, and the four weight vectors, which no kernel writes, are fetched before the wait for the kernel in front.
+template <typename TD, typename TO>
+__global__ void __launch_bounds__(LN_THREADS)
+add_layernorm_regs_kernel(float* __restrict__ residual, const TD* __restrict__ delta, int ld_delta,
+                          const float* __restrict__ after_w, const float* __restrict__ after_b, float after_eps, float mult,
+                          const float* __restrict__ norm_w, const float* __restrict__ norm_b, float norm_eps,
+                          TO* __restrict__ out, int width) {
+    __shared__ float scratch[32];
+    const int c = threadIdx.x * 8;
+    const bool mine = c < width;
+    float aw[8], ab[8], nw[8], nb[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { aw[e] = 1.f; ab[e] = 0.f; nw[e] = 1.f; nb[e] = 0.f; }
+    if (mine) {
+        if (delta != nullptr && after_w != nullptr) {
+            load8(after_w + c, aw);
+            if (after_b != nullptr) load8(after_b + c, ab);
+        }
+        if (norm_w != nullptr) {
+            load8(norm_w + c, nw);
+            if (norm_b != nullptr) load8(norm_b + c, nb);
+        }
+    }
+    pdl_wait();
+    pdl_launch_dependents();
+    float* res = residual + (size_t)blockIdx.x * width;
+    float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (mine) load8(res + c, r);
+    const float inv_width = 1.f / (float)width;
+    if (delta != nullptr) {
+        float d[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (mine) load8(delta + (size_t)blockIdx.x * ld_delta + c, d);
+        if (after_w != nullptr) {
+            float s = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s += d[e];
+            const float mean = block_sum(s, scratch) * inv_width;
+            float q = 0.f;
+            if (mine) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) { d[e] -= mean; q += d[e] * d[e]; }
+            }
+            const float rstd = rsqrtf(block_sum(q, scratch) * inv_width + after_eps);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) d[e] = d[e] * rstd * aw[e] + ab[e];
+        }
+        if (mine) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) r[e] += mult * d[e];
+            store8(res + c, r);
+        }
+    }
+    if (norm_w == nullptr) return;
+    float s = 0.f;
+    if (mine) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s += r[e];
+    }
+    const float mean = block_sum(s, scratch) * inv_width;
+    float q = 0.f;
+    if (mine) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { r[e] -= mean; q += r[e] * r[e]; }
+    }
+    const float rstd = rsqrtf(block_sum(q, scratch) * inv_width + norm_eps);
+    if (mine) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = r[e] * rstd * nw[e] + nb[e];
+        store8(out + (size_t)blockIdx.x * width + c, o);
+    }
+}
+
 // delta: null, float32 or bfloat16 [rows, ld_delta]; weights and biases float32; out: float32 or bfloat16 (null with norm_w null).
 TTB_EXPORT int ttb_add_layernorm(float* residual, const void* delta, int delta_dtype, int ld_delta, const float* after_w,
                                  const float* after_b, float after_eps, float mult, const float* norm_w,
@@ -66,8 +141,17 @@ TTB_EXPORT int ttb_add_layernorm(float* residual, const void* delta, int delta_d
     if (!residual || width < 1 || (norm_w && !out)) return TTB_ERR_ARGUMENT;
     const size_t smem = (size_t)width * sizeof(float);
     if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
+    // rows that fit a thread's registers: width a multiple of 8 up to LN_THREADS * 8, everything 16-byte aligned
+    const bool regs = (width & 7) == 0 && width <= LN_THREADS * 8 && aligned16(residual) && (!delta || (aligned16(delta) && (ld_delta & 7) == 0)) &&
+                      (!after_w || aligned16(after_w)) && (!after_b || aligned16(after_b)) && (!norm_w || aligned16(norm_w)) &&
+                      (!norm_b || aligned16(norm_b)) && (!out || aligned16(out));
 #define LN_LAUNCH(TD, TO)                                                                                            \
     do {                                                                                                             \
+        if (regs) {                                                                                                  \
+            ttb_launch(add_layernorm_regs_kernel<TD, TO>, rows, LN_THREADS, 0, stream, residual, (const TD*)delta, ld_delta, \
+                       after_w, after_b, after_eps, mult, norm_w, norm_b, norm_eps, (TO*)out, width);                \
+            break;                                                                                                   \
+        }                                                                                                            \
         if (smem > 48 * 1024)                                                                                        \
             cudaFuncSetAttribute(add_layernorm_kernel<TD, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
         ttb_launch(add_layernorm_kernel<TD, TO>, rows, LN_THREADS, smem, stream, residual, (const TD*)delta, ld_delta,    \
