@@ -329,6 +329,11 @@ latent_out_kernel(const T* __restrict__ mixed, const float* __restrict__ partial
                   T* __restrict__ out, int heads, int latent, int vdim) {
     extern __shared__ __align__(16) float lo_c[];          // [latent]
     __shared__ float wt[64];
+    {   // this head's W_uv on its way into L2 while the attention kernel finishes
+        const char* w = reinterpret_cast<const char*>(w_uv + (size_t)blockIdx.y * vdim * latent);
+        const size_t bytes = (size_t)vdim * latent * sizeof(T);
+        for (size_t off = (size_t)threadIdx.x * 128; off < bytes; off += (size_t)LO_THREADS * 128) prefetch_l2(w + off);
+    }
     pdl_wait();
     pdl_launch_dependents();
     const int t = blockIdx.x, h = blockIdx.y;

@@ -29,6 +29,12 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
     float* h = rt_smem;                                   // [TPB, wpad]
     float* z = h + TPB * wpad;                            // [TPB, experts + 1]
     int* taken = reinterpret_cast<int*>(z + TPB * (experts + 1));    // [TPB, experts]
+    if (TPB == 1) {      // a handful of tokens: the router's matrix on its way into L2 while the norm in front finishes
+        const char* w = reinterpret_cast<const char*>(w_router);
+        const size_t bytes = (size_t)(experts + (shared ? 1 : 0)) * width * sizeof(float);
+        for (size_t off = (size_t)(blockIdx.x * blockDim.x + threadIdx.x) * 128; off < bytes; off += (size_t)gridDim.x * blockDim.x * 128)
+            prefetch_l2(w + off);
+    }
     pdl_wait();
     pdl_launch_dependents();
     const int t0 = blockIdx.x * TPB, nt = min(TPB, tokens - t0);
