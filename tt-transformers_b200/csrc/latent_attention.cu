@@ -324,8 +324,9 @@ TTB_EXPORT int ttb_gate_heads(const void* in, long long stride_t, long long stri
 
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(LO_THREADS)
-latent_out_kernel(const T* __restrict__ mixed, const float* __restrict__ partial_o, const float* __restrict__ partial_ml,
-                  int splits, const T* __restrict__ w_uv, const float* __restrict__ gate, int ld_gate, int per_head,
+latent_out_kernel(const T* __restrict__ mixed, long long in_stride_t, long long in_stride_h,
+                  const float* __restrict__ partial_o, const float* __restrict__ partial_ml, int splits,
+                  const T* __restrict__ w_uv, const float* __restrict__ gate, int ld_gate, int per_head,
                   T* __restrict__ out, int heads, int latent, int vdim) {
     extern __shared__ __align__(16) float lo_c[];          // [latent]
     __shared__ float wt[64];
@@ -365,7 +366,8 @@ latent_out_kernel(const T* __restrict__ mixed, const float* __restrict__ partial
             lo_c[c] = acc;
         }
     } else {
-        for (int c = threadIdx.x; c < latent; c += LO_THREADS) lo_c[c] = to_float(mixed[row * latent + c]);
+        const T* src = mixed + (size_t)t * in_stride_t + (size_t)h * in_stride_h;
+        for (int c = threadIdx.x; c < latent; c += LO_THREADS) lo_c[c] = to_float(src[c]);
     }
     __syncthreads();
     const T* W = w_uv + (size_t)h * vdim * latent;
@@ -404,9 +406,10 @@ latent_out_kernel(const T* __restrict__ mixed, const float* __restrict__ partial
     }
 }
 
-// mixed: [tokens, heads, latent] (splits == 1) or null with partial_o / partial_ml as the attention kernel's key
-// splits left them (2 <= splits <= 64); w_uv: [heads, vdim, latent]; out: [tokens, heads * vdim].
-TTB_EXPORT int ttb_latent_out(const void* mixed, const float* partial_o, const float* partial_ml, int splits, const void* w_uv,
+// mixed: [tokens, heads, latent] with element strides (in_stride_t, in_stride_h, 1) (splits == 1), or null with
+// partial_o / partial_ml as the attention kernel's key splits left them (2 <= splits <= 64); w_uv: [heads, vdim, latent];
+// out: [tokens, heads * vdim]. Without a gate and with one split this is a per-head matrix-vector product of any use.
+TTB_EXPORT int ttb_latent_out(const void* mixed, long long in_stride_t, long long in_stride_h, const float* partial_o, const float* partial_ml, int splits, const void* w_uv,
                               const float* gate, int ld_gate, int per_head, void* out, int dtype, int tokens, int heads,
                               int latent, int vdim, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
@@ -417,7 +420,7 @@ TTB_EXPORT int ttb_latent_out(const void* mixed, const float* partial_o, const f
     dim3 grid(tokens, heads);
     const size_t smem = (size_t)latent * sizeof(float);
 #define LO_LAUNCH(T, VEC)                                                                                            \
-    ttb_launch(latent_out_kernel<T, VEC>, grid, LO_THREADS, smem, stream, (const T*)mixed, partial_o, partial_ml, splits,  \
+    ttb_launch(latent_out_kernel<T, VEC>, grid, LO_THREADS, smem, stream, (const T*)mixed, in_stride_t, in_stride_h, partial_o, partial_ml, splits,  \
                (const T*)w_uv, gate, ld_gate, per_head, (T*)out, heads, latent, vdim)
     if (dtype == TTB_DTYPE_BF16) { if (vec) LO_LAUNCH(__nv_bfloat16, true); else LO_LAUNCH(__nv_bfloat16, false); }
     else if (dtype == TTB_DTYPE_F32) { if (vec) LO_LAUNCH(float, true); else LO_LAUNCH(float, false); }

@@ -680,7 +680,9 @@ class CudaKernels:
             per_head = 1 if gate.shape[1] == H and V != 1 else 0
         res = torch.empty(T, H * V, dtype=w_uv.dtype, device=self.device)
         self._check(self.lib.ttb_latent_out(
-            self._p(mixed), self._p(partial_o), self._p(partial_ml), splits, self._p(w_uv),
+            self._p(mixed), ctypes.c_longlong(mixed.stride(0) if mixed is not None else 0),
+            ctypes.c_longlong(mixed.stride(1) if mixed is not None else 0), self._p(partial_o), self._p(partial_ml), splits,
+            self._p(w_uv),
             self._p(gate), gate.stride(0) if gate is not None else 0, per_head, self._p(res), _dtype_code(res.dtype), T, H, R,
             V, self._stream()), "latent_out")
         return res
