@@ -302,6 +302,31 @@ def test_engine_matches_the_plain_implementation_however_the_requests_are_cut(fo
         engine.close()
 
 
+@pytest.mark.parametrize("dtype,tol", [("float32", 1e-4), ("bfloat16", 6e-2)])
+def test_a_long_prompt_whole_in_portions_and_decoded(folders, dtype, tol):
+    """700 tokens: the expert products over groups of rows, attention over many key tiles, decoding at a long context."""
+    cfg, w = cases.read_folder(folders["ALIGNED"])
+    requests = {"long": helpers.random_tokens(cfg["vocab"], 700, 5), "other": helpers.random_tokens(cfg["vocab"], 90, 6)}
+    ref = {rid: plain_bozavik.forward(cfg, w, toks) for rid, toks in requests.items()}
+    for steps in (helpers.steps_whole(requests), helpers.steps_decode_tail(requests, 40),
+                  helpers.steps_portions(requests, sizes=(130, 2, 257, 64, 3, 190)), helpers.steps_mixed(requests, decode_tail=20)):
+        pages = -(-helpers.max_live_tokens(requests, steps, rounding=16) // 16)
+        engine = build_engine(folders["ALIGNED"], EngineConfig(dtype=dtype, page_size=16, num_pages=pages, max_batch_size=2,
+                                                               max_seq_len=1024, device=DEV))
+        for g in engine.cache.groups:
+            g.storage["rows"].fill_(float("nan"))
+        got = helpers.run_steps(engine, steps)
+        engine.cache.audit()
+        for rid in ref:
+            scale = float(ref[rid].abs().max())
+            rows = (got[rid] - ref[rid]).abs().amax(dim=-1) / scale
+            if dtype == "float32":
+                assert float(rows.max()) < tol, rid
+            else:
+                assert float((rows < tol).float().mean()) >= 0.9 and float(rows.median()) < tol / 2, rid
+        engine.close()
+
+
 def test_residual_stream_after_every_layer(folders):
     """Layer by layer in float32: the model cut to its first k layers, then the final norm and head of the plain
     implementation applied to the plain residual stream at that depth."""
