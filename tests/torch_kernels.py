@@ -162,9 +162,9 @@ class TorchKernels:
             view.rows[pages, pos % P] = row.to(view.rows.dtype)
         return cq.to(out_dtype)
 
-    def heads_linear(self, x, w):
+    def heads_linear(self, x, w, out_dtype=None):
         """x [T, H, K] (any strides), w [H, N, K] -> [T, H, N]."""
-        return torch.einsum("thk,hnk->thn", x.float(), w.float()).to(x.dtype)
+        return torch.einsum("thk,hnk->thn", x.float(), w.float()).to(out_dtype or x.dtype)
 
     def latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim):
         T, H, R = q_latent.shape
@@ -236,6 +236,189 @@ class TorchKernels:
         if shared is not None:
             shared_out = self.linear(self.linear_glu_clamped(x, shared[0], shared[2], alpha), shared[1])
             out += shared_out.float() * shared_gate[:, None]
+        return out
+
+    # ------------------------------------------------------------------ the float32 stream, several outputs at once
+    def stream_add_norm(self, residual, deltas, row_vector=None, weight=None, eps=0.0, offset=0.0, out_dtype=None):
+        for d in deltas:
+            if d is not None:
+                residual += d.to(torch.float32)
+        if row_vector is not None:
+            residual += row_vector
+        if weight is None:
+            return None
+        scale = 1.0 / torch.sqrt(residual.pow(2).mean(dim=-1, keepdim=True) + eps)
+        return (residual * scale * (offset + weight.to(torch.float32))).to(out_dtype)
+
+    def gated_rmsnorm(self, x, weight, eps, gate, out_dtype):
+        scale = 1.0 / torch.sqrt(x.pow(2).mean(dim=-1, keepdim=True) + eps)
+        return (x * scale * weight * torch.sigmoid(gate.float())).to(out_dtype)
+
+    def mean_rmsnorm_pair(self, a, wa, b, wb, eps):
+        a, b = a.float(), b.float()
+        ka = 1.0 / torch.sqrt(a.pow(2).mean(dim=-1, keepdim=True) + eps)
+        kb = 1.0 / torch.sqrt(b.pow(2).mean(dim=-1, keepdim=True) + eps)
+        return 0.5 * (a * ka * wa + b * kb * wb)
+
+    @staticmethod
+    def _gelu_tanh(z):
+        return 0.5 * z * (1 + torch.tanh(0.7978845608028654 * (z + 0.044715 * z ** 3)))
+
+    def glu_activation(self, gate_up, activation):
+        inter = gate_up.shape[1] // 2
+        g, u = gate_up[:, :inter].float(), gate_up[:, inter:].float()
+        act = g * torch.sigmoid(g) if activation == "silu" else self._gelu_tanh(g)
+        return (act * u).to(gate_up.dtype)
+
+    def activation(self, x, activation, out_dtype):
+        assert activation == "relu2"
+        return torch.relu(x.float()).pow(2).to(out_dtype)
+
+    # ------------------------------------------------------------------ recurrent mixers
+    def lightning_attention(self, proj, batch, view, heads, dim, vdim, decays, write_state=True):
+        T = proj.shape[0]
+        act = proj.float()
+        act = act * torch.sigmoid(act)
+        q = act[:, :heads * dim].view(T, heads, dim)
+        k = act[:, heads * dim:2 * heads * dim].view(T, heads, dim)
+        v = act[:, 2 * heads * dim:2 * heads * dim + heads * vdim].view(T, heads, vdim)
+        out = torch.empty(T, heads, vdim, dtype=torch.float32, device=proj.device)
+        start = 0
+        for r, n in enumerate(batch.seg_lens):
+            slot = batch.seg_slot_list[r]
+            S = view.state[slot].clone()
+            for t in range(start, start + n):
+                S = decays[:, None, None] * S + k[t][:, :, None] * v[t][:, None, :]
+                out[t] = torch.einsum("hdv,hd->hv", S, q[t])
+            if write_state:
+                view.state[slot] = S
+            start += n
+        return out.reshape(T, heads * vdim)
+
+    def causal_conv(self, x, bias_x, conv_w, conv_b, batch, view):
+        T, C = x.shape
+        taps = conv_w.shape[1]
+        xin = (x.float() + bias_x).to(x.dtype).float()
+        u = torch.empty(T, C, dtype=torch.float32, device=x.device)
+        start = 0
+        for r, n in enumerate(batch.seg_lens):
+            slot = batch.seg_slot_list[r]
+            kept = view.tail[slot][:taps - 1].float() if taps > 1 else xin[:0]
+            seq = torch.cat([kept, xin[start:start + n]], 0)
+            acc = conv_b[None, :].repeat(n, 1)
+            for j in range(taps):
+                acc = acc + seq[j:j + n] * conv_w[:, j]
+            u[start:start + n] = acc
+            start += n
+        return u.to(x.dtype)
+
+    def gated_recurrence(self, u, gates, gate_bias, rate, yx, bias_yx, batch, view, write_state=True):
+        T, C = u.shape
+        B = gates.shape[1]
+        s = C // B
+        pre = gates + gate_bias
+        r = torch.sigmoid(pre[:, :, :s]).reshape(T, C)
+        i = torch.sigmoid(pre[:, :, s:]).reshape(T, C)
+        a = torch.exp(-rate * r)
+        drive = torch.sqrt((1 - a * a).clamp(min=0)) * (i * u.float())
+        y = self._gelu_tanh(yx[:, :C].float() + bias_yx[:C])
+        xin = (yx[:, C:].float() + bias_yx[C:]).to(u.dtype)
+        out = torch.empty(T, C, dtype=torch.float32, device=u.device)
+        start = 0
+        keep = view.taps - 1
+        for n, slot in zip(batch.seg_lens, batch.seg_slot_list):
+            S = view.state[slot].clone()
+            for t in range(start, start + n):
+                S = a[t] * S + drive[t]
+                out[t] = S * y[t]
+            if write_state:
+                view.state[slot] = S
+                if keep > 0:
+                    view.tail[slot][:keep] = torch.cat([view.tail[slot][:keep], xin[start:start + n]], 0)[-keep:]
+            start += n
+        return out.to(u.dtype)
+
+    # ------------------------------------------------------------------ attention with a sink, a cap, chunks
+    def qk_norm_rope_write(self, qkv, batch, q_norm, k_norm, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, view,
+                           write_kv=True):
+        T = qkv.shape[0]
+        n_qk = heads + kv_heads
+        x = qkv[:, :n_qk * dim].float().view(T, n_qk, dim)
+        if q_norm is not None:
+            x = x / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+            x = torch.cat([x[:, :heads] * q_norm, x[:, heads:] * k_norm], 1)
+        if rotary_dim:
+            half = rotary_dim // 2
+            angles = batch.positions.to(torch.float32)[:, None] * inv_freq[None, :]
+            cos, sin = torch.cos(angles)[:, None, :], torch.sin(angles)[:, None, :]
+            a, b = x[..., :half], x[..., half:rotary_dim]
+            x = torch.cat([a * cos - b * sin, b * cos + a * sin, x[..., rotary_dim:]], -1)
+        qkv[:, :n_qk * dim] = x.reshape(T, n_qk * dim).to(qkv.dtype)
+        if not write_kv or view is None:
+            return
+        P = view.page_size
+        pos = batch.positions.long()
+        pages = view.block_table[batch.seg_of_token.long(), pos // P].long()
+        view.keys[pages, :, pos % P, :] = qkv[:, heads * dim:n_qk * dim].view(T, kv_heads, dim)
+        view.values[pages, :, pos % P, :] = qkv[:, n_qk * dim:].view(T, kv_heads, vdim)
+
+    def sink_attention(self, qkv, batch, heads, kv_heads, dim, vdim, scale, softcap, sinks, view):
+        T = qkv.shape[0]
+        q_all = qkv[:, :heads * dim].float().view(T, heads, dim)
+        out = torch.empty(T, heads, vdim, dtype=torch.float32, device=qkv.device)
+        P = view.page_size
+        start = 0
+        for r, n in enumerate(batch.seg_lens):
+            pos0 = batch.seg_pos0_list[r]
+            ctx = pos0 + n
+            n_pages = -(-ctx // P)
+            pages = view.block_table[r, :n_pages].long()
+            k = view.keys[pages].permute(0, 2, 1, 3).reshape(n_pages * P, kv_heads, dim)[:ctx].float()
+            v = view.values[pages].permute(0, 2, 1, 3).reshape(n_pages * P, kv_heads, vdim)[:ctx].float()
+            rep = heads // kv_heads
+            k, v = k.repeat_interleave(rep, dim=1), v.repeat_interleave(rep, dim=1)
+            scores = torch.einsum("thd,shd->hts", q_all[start:start + n], k) * scale
+            if softcap:
+                scores = softcap * torch.tanh(scores / softcap)
+            qpos = torch.arange(pos0, ctx, device=qkv.device)[:, None]
+            kpos = torch.arange(ctx, device=qkv.device)[None, :]
+            visible = kpos <= qpos
+            if view.window:
+                visible &= kpos > qpos - view.window
+            if view.chunk:
+                visible &= (kpos // view.chunk) == (qpos // view.chunk)
+            scores = scores.masked_fill(~visible[None], float("-inf"))
+            if sinks is not None:
+                scores = torch.cat([scores, sinks[:, None, None].expand(heads, n, 1)], -1)
+            weights = torch.softmax(scores, dim=-1)[..., :ctx]
+            # pages that a chunk or a window has passed may have been given back: what they hold now has weight 0
+            v = torch.where(torch.isfinite(v), v, torch.zeros_like(v))
+            out[start:start + n] = torch.einsum("hts,shd->thd", weights, v)
+            start += n
+        return out.reshape(T, heads * vdim).to(qkv.dtype)
+
+    # ------------------------------------------------------------------ experts chosen from the best groups
+    def route_grouped(self, x, w_router, experts, top, groups, keep, floor):
+        s = torch.softmax(x.float() @ w_router.t(), dim=-1)
+        T = s.shape[0]
+        per = experts // groups
+        best = s.view(T, groups, per).max(-1).values
+        kept = torch.sort(best, dim=-1, descending=True, stable=True).indices[:, :keep]
+        allowed = torch.zeros(T, groups, dtype=torch.bool, device=x.device)
+        allowed.scatter_(1, kept, True)
+        masked = torch.where(allowed.repeat_interleave(per, 1), s, torch.full_like(s, -1.0))
+        order = torch.sort(masked, dim=-1, descending=True, stable=True).indices[:, :top]
+        chosen = torch.gather(s, 1, order)
+        return order.to(torch.int32), chosen / (chosen.sum(-1, keepdim=True) + floor)
+
+    def plain_experts(self, x, choice, weight, w_up, w_down, activation="relu2"):
+        T, top = choice.shape
+        out = torch.zeros(T, w_down.shape[1], dtype=torch.float32, device=x.device)
+        for t in range(T):
+            for j in range(top):
+                e = int(choice[t, j])
+                hidden = self.activation(self.linear(x[t:t + 1], w_up[e], out_dtype=torch.float32), activation, x.dtype)
+                out[t] += weight[t, j] * self.linear(hidden, w_down[e]).float()[0]
         return out
 
     # ------------------------------------------------------------------ sampling

@@ -78,16 +78,20 @@ class CacheManager:
         self._unit_of_entry: Dict[int, tuple] = {}             # entry -> (group index, unit index)
         by_request: Dict[object, _Group] = {}
         for entry, req in enumerate(cache_requests):
-            if req is None or isinstance(req, int):
+            if req is None or (isinstance(req, int) and not isinstance(req, bool)):
                 continue
-            if not isinstance(req, CacheRequest):
-                raise TypeError(f"layer-order entry {entry}: {req!r} is no CacheRequest")
-            if req not in by_request:
-                by_request[req] = _Group(index=len(self.groups), request=req)
-                self.groups.append(by_request[req])
-            group = by_request[req]
-            self._unit_of_entry[entry] = (group.index, len(group.units))
-            group.units.append(entry)
+            several = isinstance(req, (tuple, list))         # a mixer made of mixers: a unit for each of them
+            units = []
+            for one in (req if several else (req,)):
+                if not isinstance(one, CacheRequest):
+                    raise TypeError(f"layer-order entry {entry}: {one!r} is no CacheRequest")
+                if one not in by_request:
+                    by_request[one] = _Group(index=len(self.groups), request=one)
+                    self.groups.append(by_request[one])
+                group = by_request[one]
+                units.append((group.index, len(group.units)))
+                group.units.append(entry)
+            self._unit_of_entry[entry] = tuple(units) if several else units[0]
         for entry, req in enumerate(cache_requests):
             if isinstance(req, int) and not isinstance(req, bool):
                 if req not in self._unit_of_entry:
@@ -166,9 +170,10 @@ class CacheManager:
     def bytes_per_page(cache_requests, page_size: int, dtype: torch.dtype) -> int:
         """Device bytes that one more page costs, over all paged groups (every group has the same number of pages)."""
         total, seen = 0, {}
-        for req in cache_requests:
-            if isinstance(req, CacheRequest) and req.paged:
-                seen[req] = seen.get(req, 0) + 1
+        for entry in cache_requests:
+            for req in (entry if isinstance(entry, (tuple, list)) else (entry,)):
+                if isinstance(req, CacheRequest) and req.paged:
+                    seen[req] = seen.get(req, 0) + 1
         for req, units in seen.items():
             for shape, dt in req.storage(page_size).values():
                 count = 1
@@ -236,11 +241,16 @@ class CacheManager:
             raise ValueError("commit beyond what was reserved")
         live.length = new_length
         for g in self.groups:
-            if g.pool is None or g.request.window is None:
+            if g.pool is None or (g.request.window is None and g.request.chunk is None):
                 continue
             # the next query sits at position >= new_length and reads keys > position - window; a step
             # taken back (rollback) moves the request's end back by up to ROLLBACK_SLACK positions
-            first_needed = max(0, new_length - self.ROLLBACK_SLACK - g.request.window + 1)
+            end = max(0, new_length - self.ROLLBACK_SLACK)
+            first_needed = 0
+            if g.request.window is not None:
+                first_needed = max(0, end - g.request.window + 1)
+            if g.request.chunk is not None:                  # ... and only keys of the chunk that holds it
+                first_needed = max(first_needed, end // g.request.chunk * g.request.chunk)
             dead = first_needed // self.page_size            # pages wholly below first_needed
             row = live.pages[g.index]
             freed = [p for p in row[:dead] if p != 0]
@@ -251,7 +261,8 @@ class CacheManager:
                 g.table[live.slot, :dead] = 0
 
     def has_windows(self) -> bool:
-        return any(g.pool is not None and g.request.window is not None for g in self.groups)
+        return any(g.pool is not None and (g.request.window is not None or g.request.chunk is not None)
+                   for g in self.groups)
 
     def rollback(self, request_id, length: int) -> None:
         """Take back a step that was committed ahead of time and then not used: the request holds
@@ -288,7 +299,12 @@ class CacheManager:
         """The cache view of a layer-order entry for this step (None if it has no cache)."""
         if entry not in self._unit_of_entry:
             return None
-        gi, unit = self._unit_of_entry[entry]
+        where = self._unit_of_entry[entry]
+        if where and isinstance(where[0], tuple):            # a unit for each mixer of a mixer made of mixers
+            return tuple(self._view(gi, unit, batch) for gi, unit in where)
+        return self._view(where[0], where[1], batch)
+
+    def _view(self, gi: int, unit: int, batch):
         g = self.groups[gi]
         tensors = {name: tensor[unit] for name, tensor in g.storage.items()}
         if g.pool is not None:

@@ -9,6 +9,10 @@
 // pages [num_pages, kv_heads, page_size, head_dim] through block_table[r, position / page_size].
 // Tiles start at multiples of TILE from position 0, so that the order of summation for a
 // query does not depend on how its request was cut into steps.
+//
+// Options, all off by default: values of another size than keys (value_dim); a cap on the scores,
+// score = cap * tanh(score / cap); chunks (lo = the first position of the chunk of `chunk` positions that
+// holds p); a sink per head, one more term exp(sink_h) of the softmax's denominator without a value.
 #include "common.cuh"
 
 #define ATT_TILE 128
@@ -22,7 +26,8 @@ paged_attention_generic_kernel(const T* __restrict__ qkv, int q_row_stride, T* _
                                const T* __restrict__ key_pages, const T* __restrict__ value_pages,
                                const int* __restrict__ block_table, int table_width, int page_size,
                                int heads, int kv_heads, int head_dim, float scale, int window, int num_pages,
-                               int* __restrict__ status) {
+                               int* __restrict__ status, int value_dim, float softcap, int chunk,
+                               const float* __restrict__ sinks) {
     extern __shared__ float smem[];
     float* q = smem;                                   // [head_dim, padded to an even count]
     float* prob = smem + ((head_dim + 1) & ~1);        // [ATT_TILE]
@@ -33,7 +38,8 @@ paged_attention_generic_kernel(const T* __restrict__ qkv, int q_row_stride, T* _
     const int g = h / (heads / kv_heads);
     const int pos = positions[t];
     const int seg = seg_of_token[t];
-    const int lo = (window > 0 && pos - window + 1 > 0) ? pos - window + 1 : 0;
+    int lo = (window > 0 && pos - window + 1 > 0) ? pos - window + 1 : 0;
+    if (chunk > 0 && pos / chunk * chunk > lo) lo = pos / chunk * chunk;
     const int* table = block_table + (size_t)seg * table_width;
 
     const T* q_src = qkv + (size_t)t * q_row_stride + (size_t)h * head_dim;
@@ -58,9 +64,9 @@ paged_attention_generic_kernel(const T* __restrict__ qkv, int q_row_stride, T* _
             page = -1;
         }
         if (page >= 0) {
-            const size_t off = (((size_t)page * kv_heads + g) * page_size + (key % page_size)) * head_dim;
-            row_offset[threadIdx.x] = off;
-            const T* k = key_pages + off;
+            const size_t row = ((size_t)page * kv_heads + g) * page_size + (key % page_size);
+            row_offset[threadIdx.x] = row * value_dim;
+            const T* k = key_pages + row * head_dim;
             float dot = 0.f;
             if (vec_ok) {
                 for (int d = 0; d < head_dim; d += 8) {
@@ -73,6 +79,7 @@ paged_attention_generic_kernel(const T* __restrict__ qkv, int q_row_stride, T* _
                 for (int d = 0; d < head_dim; ++d) dot += q[d] * to_float(k[d]);
             }
             score = dot * scale;
+            if (softcap > 0.f) score = softcap * tanhf(score / softcap);
         }
         const float tile_max = block_max(score, scratch);
         const float new_max = fmaxf(run_max, tile_max);       // finite: every tile holds at least one visible key
@@ -88,31 +95,40 @@ paged_attention_generic_kernel(const T* __restrict__ qkv, int q_row_stride, T* _
 #pragma unroll
         for (int a = 0; a < ATT_MAX_ACC; ++a) {
             const int d = threadIdx.x + a * ATT_THREADS;
-            if (d < head_dim) {
+            if (d < value_dim) {
                 float sum = 0.f;
                 for (int j = k_begin; j < k_end; ++j) sum += prob[j] * to_float(value_pages[row_offset[j] + d]);
                 acc[a] = acc[a] * correction + sum;
             }
         }
     }
-    const float inv = 1.f / run_sum;
-    T* dst = out + ((size_t)t * heads + h) * head_dim;
+    float shrink = 1.f;
+    if (sinks != nullptr) {                                  // one more term of the denominator; it has no value
+        const float sink = sinks[h];
+        const float top = fmaxf(run_max, sink);
+        shrink = expf(run_max - top);
+        run_sum = run_sum * shrink + expf(sink - top);
+    }
+    const float inv = shrink / run_sum;
+    T* dst = out + ((size_t)t * heads + h) * value_dim;
 #pragma unroll
     for (int a = 0; a < ATT_MAX_ACC; ++a) {
         const int d = threadIdx.x + a * ATT_THREADS;
-        if (d < head_dim) dst[d] = from_float<T>(acc[a] * inv);
+        if (d < value_dim) dst[d] = from_float<T>(acc[a] * inv);
     }
 }
 
-TTB_EXPORT int ttb_paged_attention_generic(const void* qkv, int q_row_stride, void* out, int dtype,
+TTB_EXPORT int ttb_paged_attention_generic_ext(const void* qkv, int q_row_stride, void* out, int dtype,
                                            const int* positions, const int* seg_of_token, const void* key_pages,
                                            const void* value_pages, const int* block_table, int table_width,
                                            int page_size, int tokens, int heads, int kv_heads, int head_dim,
-                                           float scale, int window, int num_pages, int* status, cudaStream_t stream) {
+                                           float scale, int window, int num_pages, int* status, int value_dim, float softcap,
+                                           int chunk, const float* sinks, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
     if (!qkv || !out || !positions || !seg_of_token || !key_pages || !value_pages || !block_table || !status)
         return TTB_ERR_ARGUMENT;
-    if (head_dim < 1 || head_dim > ATT_MAX_ACC * ATT_THREADS) return TTB_ERR_UNSUPPORTED;
+    if (head_dim < 1 || value_dim < 1 || value_dim > ATT_MAX_ACC * ATT_THREADS || head_dim > 4096) return TTB_ERR_UNSUPPORTED;
+    if (softcap < 0.f || chunk < 0) return TTB_ERR_ARGUMENT;
     if (kv_heads < 1 || heads % kv_heads != 0) return TTB_ERR_UNSUPPORTED;
     if (heads > 65535) return TTB_ERR_UNSUPPORTED;
     const size_t smem = (size_t)(((head_dim + 1) & ~1) + ATT_TILE) * sizeof(float) + ATT_TILE * sizeof(size_t);
@@ -122,14 +138,24 @@ TTB_EXPORT int ttb_paged_attention_generic(const void* qkv, int q_row_stride, vo
         paged_attention_generic_kernel<<<grid, ATT_THREADS, smem, stream>>>(
             (const __nv_bfloat16*)qkv, q_row_stride, (__nv_bfloat16*)out, positions, seg_of_token,
             (const __nv_bfloat16*)key_pages, (const __nv_bfloat16*)value_pages, block_table, table_width, page_size,
-            heads, kv_heads, head_dim, scale, window, num_pages, status);
+            heads, kv_heads, head_dim, scale, window, num_pages, status, value_dim, softcap, chunk, sinks);
     } else if (dtype == TTB_DTYPE_F32) {
         if ((head_dim & 7) == 0 && (!aligned16(key_pages))) return TTB_ERR_ARGUMENT;
         paged_attention_generic_kernel<<<grid, ATT_THREADS, smem, stream>>>(
             (const float*)qkv, q_row_stride, (float*)out, positions, seg_of_token, (const float*)key_pages,
-            (const float*)value_pages, block_table, table_width, page_size, heads, kv_heads, head_dim, scale, window, num_pages, status);
+            (const float*)value_pages, block_table, table_width, page_size, heads, kv_heads, head_dim, scale, window, num_pages, status, value_dim, softcap, chunk, sinks);
     } else {
         return TTB_ERR_UNSUPPORTED;
     }
     return ttb_launch_status();
+}
+
+TTB_EXPORT int ttb_paged_attention_generic(const void* qkv, int q_row_stride, void* out, int dtype,
+                                           const int* positions, const int* seg_of_token, const void* key_pages,
+                                           const void* value_pages, const int* block_table, int table_width,
+                                           int page_size, int tokens, int heads, int kv_heads, int head_dim,
+                                           float scale, int window, int num_pages, int* status, cudaStream_t stream) {
+    return ttb_paged_attention_generic_ext(qkv, q_row_stride, out, dtype, positions, seg_of_token, key_pages, value_pages, block_table,
+                                           table_width, page_size, tokens, heads, kv_heads, head_dim, scale, window, num_pages, status,
+                                           head_dim, 0.f, 0, nullptr, stream);
 }

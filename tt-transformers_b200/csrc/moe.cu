@@ -525,7 +525,8 @@ __device__ __forceinline__ void mv_dots(const T* const (&w)[R], const float* __r
     for (int r = 0; r < R; ++r) out[r] = warp_sum(out[r]);
 }
 
-template <typename T, bool VEC>
+// GLU: W_e = [gate rows; up rows] and the clamped gated activation. Otherwise W_e = [rows] and hidden = relu(W_e x)^2.
+template <typename T, bool VEC, bool GLU>
 __global__ void __launch_bounds__(MV_THREADS)
 moe_gemv_first_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ W, long long w_expert_stride,
                       const int* __restrict__ choice, int experts, int top, T* __restrict__ hidden, int N, int K,
@@ -553,21 +554,37 @@ moe_gemv_first_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ W,
     if (n_begin >= N) return;
     const bool valid = is_shared || (unsigned)e < (unsigned)experts;
     const T* We = W + (size_t)(valid ? e : 0) * w_expert_stride;
-    const T* rows[2 * MV_ROWS_PER_WARP];
+    if (!GLU) {
+        const T* rows[MV_ROWS_PER_WARP];
 #pragma unroll
-    for (int i = 0; i < MV_ROWS_PER_WARP; ++i) {
-        const int n = min(n_begin + i, N - 1);             // rows past the end repeat the last one and are not stored
-        rows[2 * i] = We + (size_t)n * K;
-        rows[2 * i + 1] = We + (size_t)(N + n) * K;
-    }
-    float d[2 * MV_ROWS_PER_WARP];
-    mv_dots<T, VEC, 2 * MV_ROWS_PER_WARP>(rows, mv_x, K, lane, d);
-    if (lane < MV_ROWS_PER_WARP && n_begin + lane < N) {
-        float g = 0.f, u = 0.f;
+        for (int i = 0; i < MV_ROWS_PER_WARP; ++i) rows[i] = We + (size_t)min(n_begin + i, N - 1) * K;
+        float d[MV_ROWS_PER_WARP];
+        mv_dots<T, VEC, MV_ROWS_PER_WARP>(rows, mv_x, K, lane, d);
+        if (lane < MV_ROWS_PER_WARP && n_begin + lane < N) {
+            float z = 0.f;
 #pragma unroll
-        for (int i = 0; i < MV_ROWS_PER_WARP; ++i)
-            if (lane == i) { g = d[2 * i]; u = d[2 * i + 1]; }
-        hidden[(size_t)p * N + n_begin + lane] = from_float<T>(valid ? glu_clamped(g, u, limit, alpha) : 0.f);
+            for (int i = 0; i < MV_ROWS_PER_WARP; ++i)
+                if (lane == i) z = d[i];
+            z = fmaxf(z, 0.f);
+            hidden[(size_t)p * N + n_begin + lane] = from_float<T>(valid ? z * z : 0.f);
+        }
+    } else {
+        const T* rows[2 * MV_ROWS_PER_WARP];
+#pragma unroll
+        for (int i = 0; i < MV_ROWS_PER_WARP; ++i) {
+            const int n = min(n_begin + i, N - 1);             // rows past the end repeat the last one and are not stored
+            rows[2 * i] = We + (size_t)n * K;
+            rows[2 * i + 1] = We + (size_t)(N + n) * K;
+        }
+        float d[2 * MV_ROWS_PER_WARP];
+        mv_dots<T, VEC, 2 * MV_ROWS_PER_WARP>(rows, mv_x, K, lane, d);
+        if (lane < MV_ROWS_PER_WARP && n_begin + lane < N) {
+            float g = 0.f, u = 0.f;
+#pragma unroll
+            for (int i = 0; i < MV_ROWS_PER_WARP; ++i)
+                if (lane == i) { g = d[2 * i]; u = d[2 * i + 1]; }
+            hidden[(size_t)p * N + n_begin + lane] = from_float<T>(valid ? glu_clamped(g, u, limit, alpha) : 0.f);
+        }
     }
 }
 
@@ -629,11 +646,35 @@ moe_gemv_second_kernel(const T* __restrict__ hidden, const T* __restrict__ W, lo
 // [tokens * top, inter] of the compute type; out float32 [tokens, width]. The shared expert either comes as its
 // finished output (shared_out, compute type) or as its weights (shared_gate_up [2 shared_inter, width], shared_down
 // [width, shared_inter], scratch shared_hidden [tokens, shared_inter]) and then runs inside the two kernels; or not at all.
+// ttb_moe_gemv_plain: experts without a gate, y = W_down relu(W_up x)^2, w_up [experts, inter, width]; no shared expert.
+static int moe_gemv_launch(const void* x, int ldx, const void* w_gate_up, const void* w_down, const int* choice,
+                           const float* weight, void* hidden, const void* shared_out, const float* shared_gate, float* out,
+                           int dtype, int tokens, int experts, int top, int inter, int width, float limit, float alpha,
+                           const void* shared_gate_up, const void* shared_down, void* shared_hidden, int shared_inter,
+                           float shared_limit, bool glu, cudaStream_t stream);
+
+TTB_EXPORT int ttb_moe_gemv_plain(const void* x, int ldx, const void* w_up, const void* w_down, const int* choice,
+                                  const float* weight, void* hidden, float* out, int dtype, int tokens, int experts, int top,
+                                  int inter, int width, cudaStream_t stream) {
+    return moe_gemv_launch(x, ldx, w_up, w_down, choice, weight, hidden, nullptr, nullptr, out, dtype, tokens, experts, top, inter,
+                           width, 0.f, 0.f, nullptr, nullptr, nullptr, 0, 0.f, false, stream);
+}
+
 TTB_EXPORT int ttb_moe_gemv(const void* x, int ldx, const void* w_gate_up, const void* w_down, const int* choice,
                             const float* weight, void* hidden, const void* shared_out, const float* shared_gate, float* out,
                             int dtype, int tokens, int experts, int top, int inter, int width, float limit, float alpha,
                             const void* shared_gate_up, const void* shared_down, void* shared_hidden, int shared_inter,
                             float shared_limit, cudaStream_t stream) {
+    return moe_gemv_launch(x, ldx, w_gate_up, w_down, choice, weight, hidden, shared_out, shared_gate, out, dtype, tokens, experts,
+                           top, inter, width, limit, alpha, shared_gate_up, shared_down, shared_hidden, shared_inter, shared_limit,
+                           true, stream);
+}
+
+static int moe_gemv_launch(const void* x, int ldx, const void* w_gate_up, const void* w_down, const int* choice,
+                           const float* weight, void* hidden, const void* shared_out, const float* shared_gate, float* out,
+                           int dtype, int tokens, int experts, int top, int inter, int width, float limit, float alpha,
+                           const void* shared_gate_up, const void* shared_down, void* shared_hidden, int shared_inter,
+                           float shared_limit, bool glu, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
     if (!x || !w_gate_up || !w_down || !choice || !weight || !hidden || !out) return TTB_ERR_ARGUMENT;
     if ((shared_out || shared_gate_up) && !shared_gate) return TTB_ERR_ARGUMENT;
@@ -646,12 +687,17 @@ TTB_EXPORT int ttb_moe_gemv(const void* x, int ldx, const void* w_gate_up, const
     const int per_block = (MV_THREADS / 32) * MV_ROWS_PER_WARP;
     const int widest = inter > sk ? inter : sk;
     dim3 g1((widest + per_block - 1) / per_block, pairs + (shared_gate_up ? tokens : 0)), g2((width + per_block - 1) / per_block, tokens);
-    const long long s1 = 2LL * inter * width, s2 = (long long)width * inter;
+    const long long s1 = (glu ? 2LL : 1LL) * inter * width, s2 = (long long)width * inter;
 #define MV_LAUNCH(T, VEC)                                                                                            \
     do {                                                                                                             \
-        ttb_launch(moe_gemv_first_kernel<T, VEC>, g1, MV_THREADS, smem1, stream, (const T*)x, ldx, (const T*)w_gate_up, s1, \
-                   choice, experts, top, (T*)hidden, inter, width, limit, alpha, pairs, (const T*)shared_gate_up,    \
-                   (T*)shared_hidden, sk, shared_limit);                                                             \
+        if (glu)                                                                                                     \
+            ttb_launch(moe_gemv_first_kernel<T, VEC, true>, g1, MV_THREADS, smem1, stream, (const T*)x, ldx, (const T*)w_gate_up, s1, \
+                       choice, experts, top, (T*)hidden, inter, width, limit, alpha, pairs, (const T*)shared_gate_up, \
+                       (T*)shared_hidden, sk, shared_limit);                                                         \
+        else                                                                                                         \
+            ttb_launch(moe_gemv_first_kernel<T, VEC, false>, g1, MV_THREADS, smem1, stream, (const T*)x, ldx, (const T*)w_gate_up, s1, \
+                       choice, experts, top, (T*)hidden, inter, width, limit, alpha, pairs, (const T*)shared_gate_up, \
+                       (T*)shared_hidden, sk, shared_limit);                                                         \
         ttb_launch(moe_gemv_second_kernel<T, VEC>, g2, MV_THREADS, smem2, stream, (const T*)hidden, (const T*)w_down, s2,  \
                    choice, weight, experts, top, (const T*)shared_out, shared_gate, out, width, inter,               \
                    (const T*)(shared_gate_up ? shared_down : nullptr), (const T*)shared_hidden, sk);                 \

@@ -1,0 +1,133 @@
+// A gated linear recurrence per channel behind a short causal convolution, with its state per request.
+//
+// causal_conv: u[t, c] = b_c[c] + sum_j w[c, j] * x(t - taps + 1 + j, c), x(s, c) = round(x'[s, c] + b_x[c]) for tokens of
+//   this step and the request's kept inputs (tail [slots, taps - 1, channels], oldest first; zeros at a request's start)
+//   for positions before it. One thread per (token, channel); nothing is written but u, so that every block sees the
+//   tail as the step before left it.
+// gated_recurrence: one thread per (segment, channel) walks the segment's tokens in order:
+//   a = exp(-rate[c] * sigmoid(gr + br));  S = a S + sqrt(1 - a^2) * sigmoid(gi + bi) * u;  out = S * gelu_tanh(y' + b_y)
+//   with the gates' float32 pre-activations [tokens, blocks, 2 s] (decay rows, then input rows, per block). At the end
+//   it stores S and the convolution's new tail (the last taps - 1 inputs of what the request has seen).
+// Gates, decays, the state and the recurrence are float32.
+#include "common.cuh"
+
+#define RC_THREADS 128
+#define RC_MAX_TAPS 16
+
+__device__ __forceinline__ float rc_gelu_tanh(float z) {
+    return 0.5f * z * (1.f + tanhf(0.7978845608028654f * (z + 0.044715f * z * z * z)));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(RC_THREADS)
+causal_conv_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ bias_x, const float* __restrict__ w,
+                   const float* __restrict__ bias_c, const int* __restrict__ seg_of_token, const int* __restrict__ cu_seqlens,
+                   const int* __restrict__ seg_slot, const T* __restrict__ tail, T* __restrict__ u, int channels, int taps) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t = blockIdx.y, c = blockIdx.x * RC_THREADS + threadIdx.x;
+    if (c >= channels) return;
+    const int seg = seg_of_token[t];
+    const int start = cu_seqlens[seg];
+    const T* kept = tail + (size_t)seg_slot[seg] * (taps > 1 ? taps - 1 : 1) * channels;
+    const float bx = bias_x[c];
+    float acc = bias_c[c];
+    for (int j = 0; j < taps; ++j) {
+        const int s = t - (taps - 1) + j;                      // flat index of the input this tap reads
+        float v;
+        if (s >= start) v = to_float(from_float<T>(to_float(x[(size_t)s * ldx + c]) + bx));
+        else v = to_float(kept[(size_t)((taps - 1) + (s - start)) * channels + c]);
+        acc = fmaf(w[(size_t)c * taps + j], v, acc);
+    }
+    u[(size_t)t * channels + c] = from_float<T>(acc);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(RC_THREADS)
+gated_recurrence_kernel(const T* __restrict__ u, const float* __restrict__ gates, long long gate_ld_token,
+                        long long gate_ld_block, const float* __restrict__ gate_bias,
+                        const float* __restrict__ rate, const T* __restrict__ yx, int ldyx, const float* __restrict__ bias_yx,
+                        const int* __restrict__ cu_seqlens, const int* __restrict__ seg_slot, float* __restrict__ state,
+                        T* __restrict__ tail, T* __restrict__ out, int channels, int block_size, int taps, int write_state) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int seg = blockIdx.y, c = blockIdx.x * RC_THREADS + threadIdx.x;
+    if (c >= channels) return;
+    const int t_begin = cu_seqlens[seg], t_end = cu_seqlens[seg + 1];
+    if (t_begin >= t_end) return;
+    const int slot = seg_slot[seg];
+    const int b = c / block_size, i = c % block_size;
+    const size_t g_r = (size_t)b * 2 * block_size + i, g_i = g_r + block_size;     // within a token's 2 * channels gates
+    const float br = gate_bias[g_r], bi = gate_bias[g_i], k = rate[c], by = bias_yx[c];
+    const float* gate_r = gates + (size_t)b * gate_ld_block + i;                   // the product may be strided by token and block
+    const float* gate_i = gate_r + block_size;
+    float S = state[(size_t)slot * channels + c];
+#pragma unroll 4
+    for (int t = t_begin; t < t_end; ++t) {
+        const float gr = gate_r[(size_t)t * gate_ld_token] + br, gi = gate_i[(size_t)t * gate_ld_token] + bi;
+        const float r = 1.f / (1.f + expf(-gr)), in = 1.f / (1.f + expf(-gi));
+        const float log_a = -k * r;
+        const float a = expf(log_a);
+        const float mult = sqrtf(fmaxf(1.f - a * a, 0.f));
+        S = fmaf(a, S, mult * (in * to_float(u[(size_t)t * channels + c])));
+        const float y = rc_gelu_tanh(to_float(yx[(size_t)t * ldyx + c]) + by);
+        out[(size_t)t * channels + c] = from_float<T>(S * y);
+    }
+    if (!write_state) return;
+    state[(size_t)slot * channels + c] = S;
+    if (taps > 1) {
+        // the kept inputs followed by this step's: the last taps - 1 of them stay
+        const int keep = taps - 1, len = t_end - t_begin;
+        const float bx = bias_yx[channels + c];
+        T* kept = tail + (size_t)slot * keep * channels;
+        T fresh[RC_MAX_TAPS];
+        for (int j = 0; j < keep; ++j) {
+            const int at = len + j;                            // index in (kept ++ new)
+            fresh[j] = at < keep ? kept[(size_t)at * channels + c]
+                                 : from_float<T>(to_float(yx[(size_t)(t_begin + at - keep) * ldyx + channels + c]) + bx);
+        }
+        for (int j = 0; j < keep; ++j) kept[(size_t)j * channels + c] = fresh[j];
+    }
+}
+
+// x: the convolution's input before its bias, [tokens, ldx] (a slice of a wider product); u: [tokens, channels].
+TTB_EXPORT int ttb_causal_conv(const void* x, int dtype, int ldx, const float* bias_x, const float* w, const float* bias_c,
+                               const int* seg_of_token, const int* cu_seqlens, const int* seg_slot, const void* tail, void* u,
+                               int tokens, int channels, int taps, cudaStream_t stream) {
+    if (tokens == 0) return TTB_OK;
+    if (!x || !bias_x || !w || !bias_c || !seg_of_token || !cu_seqlens || !seg_slot || !tail || !u) return TTB_ERR_ARGUMENT;
+    if (taps < 1 || taps > RC_MAX_TAPS || channels < 1 || tokens > 65535) return TTB_ERR_UNSUPPORTED;
+    dim3 grid((channels + RC_THREADS - 1) / RC_THREADS, tokens);
+    if (dtype == TTB_DTYPE_BF16)
+        ttb_launch(causal_conv_kernel<__nv_bfloat16>, grid, RC_THREADS, 0, stream, (const __nv_bfloat16*)x, ldx, bias_x, w, bias_c,
+                   seg_of_token, cu_seqlens, seg_slot, (const __nv_bfloat16*)tail, (__nv_bfloat16*)u, channels, taps);
+    else if (dtype == TTB_DTYPE_F32)
+        ttb_launch(causal_conv_kernel<float>, grid, RC_THREADS, 0, stream, (const float*)x, ldx, bias_x, w, bias_c, seg_of_token,
+                   cu_seqlens, seg_slot, (const float*)tail, (float*)u, channels, taps);
+    else return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}
+
+// yx [tokens, ldyx]: the gate branch's product in columns 0 .. channels-1, the convolution's input in the next `channels`;
+// bias_yx [2 channels] likewise. gates float32 [tokens, blocks, 2 s] (per block: decay rows, input rows) with element
+// strides gate_ld_token and gate_ld_block.
+TTB_EXPORT int ttb_gated_recurrence(const void* u, int dtype, const float* gates, long long gate_ld_token, long long gate_ld_block,
+                                    const float* gate_bias, const float* rate,
+                                    const void* yx, int ldyx, const float* bias_yx, const int* cu_seqlens, const int* seg_slot,
+                                    float* state, void* tail, void* out, int segments, int channels, int blocks, int taps,
+                                    int write_state, cudaStream_t stream) {
+    if (segments == 0) return TTB_OK;
+    if (!u || !gates || !gate_bias || !rate || !yx || !bias_yx || !cu_seqlens || !seg_slot || !state || !tail || !out)
+        return TTB_ERR_ARGUMENT;
+    if (taps < 1 || taps > RC_MAX_TAPS || blocks < 1 || channels % blocks || segments > 65535) return TTB_ERR_UNSUPPORTED;
+    dim3 grid((channels + RC_THREADS - 1) / RC_THREADS, segments);
+    if (dtype == TTB_DTYPE_BF16)
+        ttb_launch(gated_recurrence_kernel<__nv_bfloat16>, grid, RC_THREADS, 0, stream, (const __nv_bfloat16*)u, gates, gate_ld_token, gate_ld_block, gate_bias, rate,
+                   (const __nv_bfloat16*)yx, ldyx, bias_yx, cu_seqlens, seg_slot, state, (__nv_bfloat16*)tail, (__nv_bfloat16*)out,
+                   channels, channels / blocks, taps, write_state);
+    else if (dtype == TTB_DTYPE_F32)
+        ttb_launch(gated_recurrence_kernel<float>, grid, RC_THREADS, 0, stream, (const float*)u, gates, gate_ld_token, gate_ld_block, gate_bias, rate, (const float*)yx,
+                   ldyx, bias_yx, cu_seqlens, seg_slot, state, (float*)tail, (float*)out, channels, channels / blocks, taps, write_state);
+    else return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}

@@ -97,7 +97,9 @@ class CudaKernels:
                      "ttb_latent_attention_generic", "ttb_gate_heads", "ttb_gemm_simt_batched", "ttb_route_top",
                      "ttb_moe_align", "ttb_moe_group_gemm", "ttb_moe_combine", "ttb_glu_clamped",
                      "ttb_latent_attention_mma", "ttb_latent_attention_mma_supports", "ttb_moe_gemv", "ttb_moe_gemm_tcgen05", "ttb_latent_out",
-                     "ttb_latent_attention_mma_tokens_per_tile"):
+                     "ttb_latent_attention_mma_tokens_per_tile", "ttb_stream_add_norm", "ttb_gated_rmsnorm",
+                     "ttb_mean_rmsnorm_pair", "ttb_activation", "ttb_lightning_scan", "ttb_causal_conv", "ttb_gated_recurrence",
+                     "ttb_paged_attention_generic_ext", "ttb_qk_norm_rope_write", "ttb_route_grouped", "ttb_moe_gemv_plain"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -631,18 +633,21 @@ class CudaKernels:
     MOE_GEMV_PAIRS = 64          # up to this many (token, choice) pairs the experts run as matrix-vector products
     HEADS_LIBRARY_ROWS = 32      # per-head bfloat16 products with at least this many rows go to the library's batched product
 
-    def heads_linear(self, x, w):
+    def heads_linear(self, x, w, out_dtype=None):
         """x [T, H, K] (any token and head strides) times w [H, N, K], head by head -> [T, H, N] (a view that may
-        be strided; its last axis is contiguous)."""
+        be strided; its last axis is contiguous). out_dtype: float32 keeps the float32 sums of a bfloat16 product."""
         T, H, K = x.shape
         N = w.shape[1]
+        out_dtype = out_dtype or x.dtype
         if w.shape[0] != H or w.shape[2] != K or x.dtype != w.dtype or x.stride(2) != 1 or not w.is_contiguous():
             raise KernelError(f"heads_linear: x {tuple(x.shape)} does not match w {tuple(w.shape)}")
         if x.dtype == torch.bfloat16 and T >= self.HEADS_LIBRARY_ROWS:
-            return torch.bmm(x.transpose(0, 1), w.transpose(1, 2)).transpose(0, 1)       # library product (cuBLAS)
-        out = torch.empty(T, H, N, dtype=x.dtype, device=self.device)
+            if out_dtype == torch.bfloat16:
+                return torch.bmm(x.transpose(0, 1), w.transpose(1, 2)).transpose(0, 1)       # library product (cuBLAS)
+            return torch.bmm(x.transpose(0, 1), w.transpose(1, 2), out_dtype=out_dtype).transpose(0, 1)
+        out = torch.empty(T, H, N, dtype=out_dtype, device=self.device)
         self._check(self.lib.ttb_gemm_simt_batched(
-            self._p(x), self._p(w), self._p(out), _dtype_code(x.dtype), _dtype_code(x.dtype), H, T, N, K, x.stride(0), K,
+            self._p(x), self._p(w), self._p(out), _dtype_code(x.dtype), _dtype_code(out_dtype), H, T, N, K, x.stride(0), K,
             H * N, ctypes.c_longlong(x.stride(1)), ctypes.c_longlong(N * K), ctypes.c_longlong(N), self._stream()),
             "heads_linear")
         return out
@@ -849,6 +854,251 @@ class CudaKernels:
             _dtype_code(shared_out.dtype) if shared_out is not None else 0, self._p(shared_gate), self._p(out), T, width,
             self._stream()), "moe_combine")
         return out
+
+    # ------------------------------------------------------------------ the float32 stream, several outputs at once
+    def stream_add_norm(self, residual, deltas, row_vector=None, weight=None, eps=0.0, offset=0.0, out_dtype=None):
+        """residual += sum(deltas) + row_vector, in place and in float32 (each delta [rows, width], float32 or
+        bfloat16; row_vector float32 [width], the same for every row); then, with a weight,
+        residual / sqrt(mean(residual^2) + eps) * (offset + weight) in out_dtype comes back (None without)."""
+        rows, width = residual.shape
+        if residual.dtype != torch.float32 or not residual.is_contiguous():
+            raise KernelError("the residual stream is float32 and contiguous")
+        deltas = [d for d in deltas if d is not None]
+        for d in deltas:
+            if d.shape != residual.shape or not d.is_contiguous():
+                raise KernelError("stream_add_norm: every delta must be contiguous and have the stream's shape")
+        out = None
+        while True:
+            now, deltas = deltas[:2], deltas[2:]
+            last = not deltas
+            d1 = now[0] if len(now) > 0 else None
+            d2 = now[1] if len(now) > 1 else None
+            if last and weight is not None:
+                out = torch.empty(rows, width, dtype=out_dtype, device=self.device)
+            if not last or d1 is not None or row_vector is not None or out is not None:
+                self._check(self.lib.ttb_stream_add_norm(
+                    self._p(residual), self._p(d1), _dtype_code(d1.dtype) if d1 is not None else 0, self._p(d2),
+                    _dtype_code(d2.dtype) if d2 is not None else 0, self._p(row_vector if last else None),
+                    self._p(weight if last else None), _dtype_code(weight.dtype) if weight is not None else 0,
+                    ctypes.c_float(offset), ctypes.c_float(eps), self._p(out), _dtype_code(out_dtype) if out is not None else 0,
+                    rows, width, self._stream()), "stream_add_norm")
+            if last:
+                return out
+
+    def gated_rmsnorm(self, x, weight, eps, gate, out_dtype):
+        """x float32 [rows, width] / sqrt(mean(x^2) + eps) * weight * sigmoid(gate) -> out_dtype; gate [rows, width] may be
+        a slice of a wider tensor (its columns contiguous)."""
+        rows, width = x.shape
+        if x.dtype != torch.float32 or not x.is_contiguous() or gate.shape != x.shape or gate.stride(1) != 1:
+            raise KernelError("gated_rmsnorm: x must be float32 and contiguous, the gate of its shape")
+        out = torch.empty(rows, width, dtype=out_dtype, device=self.device)
+        self._check(self.lib.ttb_gated_rmsnorm(self._p(x), self._p(gate), _dtype_code(gate.dtype), gate.stride(0),
+                                               self._p(weight), ctypes.c_float(eps), self._p(out), _dtype_code(out_dtype),
+                                               rows, width, self._stream()), "gated_rmsnorm")
+        return out
+
+    def mean_rmsnorm_pair(self, a, wa, b, wb, eps):
+        """(rms(a) * wa + rms(b) * wb) / 2 -> float32 [rows, width]."""
+        if a.shape != b.shape or a.dtype != b.dtype or not a.is_contiguous() or not b.is_contiguous():
+            raise KernelError("mean_rmsnorm_pair: both inputs must be contiguous and alike")
+        rows, width = a.shape
+        out = torch.empty(rows, width, dtype=torch.float32, device=self.device)
+        self._check(self.lib.ttb_mean_rmsnorm_pair(self._p(a), self._p(b), _dtype_code(a.dtype), self._p(wa), self._p(wb),
+                                                   ctypes.c_float(eps), self._p(out), rows, width, self._stream()),
+                    "mean_rmsnorm_pair")
+        return out
+
+    _ACTIVATIONS = {"silu": 0, "gelu_tanh": 1, "relu2": 2}
+
+    def glu_activation(self, gate_up, activation):
+        """act(gate) * up over [rows, gate | up] -> [rows, columns / 2]; activation "silu" or "gelu_tanh"."""
+        rows, two = gate_up.shape
+        if gate_up.stride(1) != 1 or activation not in ("silu", "gelu_tanh"):
+            raise KernelError("glu_activation: the product must be contiguous along its columns; silu or gelu_tanh")
+        out = torch.empty(rows, two // 2, dtype=gate_up.dtype, device=self.device)
+        self._check(self.lib.ttb_activation(self._p(gate_up), _dtype_code(gate_up.dtype), gate_up.stride(0), self._p(out),
+                                            _dtype_code(out.dtype), rows, two // 2, self._ACTIVATIONS[activation],
+                                            self._stream()), "glu_activation")
+        return out
+
+    def activation(self, x, activation, out_dtype):
+        """An activation element by element ("relu2": relu(z)^2), computed in float32 -> out_dtype."""
+        rows, cols = x.shape
+        if x.stride(1) != 1 or activation != "relu2":
+            raise KernelError("activation: contiguous columns; relu2")
+        out = torch.empty(rows, cols, dtype=out_dtype, device=self.device)
+        self._check(self.lib.ttb_activation(self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(out), _dtype_code(out_dtype),
+                                            rows, cols, self._ACTIVATIONS[activation], self._stream()), "activation")
+        return out
+
+    # ------------------------------------------------------------------ recurrent mixers
+    def lightning_attention(self, proj, batch, view, heads, dim, vdim, decays, write_state=True):
+        """proj [T, q | k | v | ...] before their silu; the state float32 [slots, heads, dim, vdim] of view continues
+        per segment: S = decay S + k v^T, o = S^T q. -> float32 [T, heads * vdim]."""
+        tokens = proj.shape[0]
+        if proj.stride(1) != 1 or proj.shape[1] < heads * (2 * dim + vdim):
+            raise KernelError("lightning_attention: the projection must hold q, k and v, contiguous along its columns")
+        if view.state.dtype != torch.float32 or tuple(view.state.shape[1:]) != (heads, dim, vdim) or not view.state.is_contiguous():
+            raise KernelError("lightning_attention: the state must be float32 [slots, heads, dim, vdim]")
+        out = torch.empty(tokens, heads * vdim, dtype=torch.float32, device=self.device)
+        self._check(self.lib.ttb_lightning_scan(
+            self._p(proj), _dtype_code(proj.dtype), proj.stride(0), self._p(batch.cu_seqlens), self._p(view.slots),
+            self._p(view.state), self._p(decays), self._p(out), batch.num_segments, heads, dim, vdim, 1 if write_state else 0,
+            self._stream()), "lightning_scan")
+        return out
+
+    def causal_conv(self, x, bias_x, conv_w, conv_b, batch, view):
+        """u[t] = conv_b + sum_j conv_w[:, j] * (x + bias_x)[t - taps + 1 + j] per channel, reading the request's kept
+        inputs (view.tail) before the step's first token. x [T, channels] may be a slice of a wider product."""
+        tokens, channels = x.shape
+        taps = conv_w.shape[1]
+        if x.stride(1) != 1 or view.tail.dtype != x.dtype or not view.tail.is_contiguous():
+            raise KernelError("causal_conv: contiguous columns, and kept inputs of the compute dtype")
+        u = torch.empty(tokens, channels, dtype=x.dtype, device=self.device)
+        self._check(self.lib.ttb_causal_conv(
+            self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(bias_x), self._p(conv_w), self._p(conv_b),
+            self._p(batch.seg_of_token), self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.tail), self._p(u),
+            tokens, channels, taps, self._stream()), "causal_conv")
+        return u
+
+    def gated_recurrence(self, u, gates, gate_bias, rate, yx, bias_yx, batch, view, write_state=True):
+        """a = exp(-rate * sigmoid(gates_r + b)); S = a S + sqrt(1 - a^2) * sigmoid(gates_i + b) * u;
+        out = S * gelu_tanh(yx[:, :C] + bias_yx[:C]). Leaves S and the convolution's last inputs (yx[:, C:] + bias) in
+        the request's slot. gates float32 [T, blocks, 2 s]."""
+        tokens, channels = u.shape
+        blocks = gates.shape[1]
+        if gates.dtype != torch.float32 or gates.stride(2) != 1 or not u.is_contiguous() or yx.stride(1) != 1:
+            raise KernelError("gated_recurrence: float32 gates contiguous along their last axis, contiguous u")
+        out = torch.empty(tokens, channels, dtype=u.dtype, device=self.device)
+        self._check(self.lib.ttb_gated_recurrence(
+            self._p(u), _dtype_code(u.dtype), self._p(gates), ctypes.c_longlong(gates.stride(0)),
+            ctypes.c_longlong(gates.stride(1)), self._p(gate_bias), self._p(rate), self._p(yx), yx.stride(0),
+            self._p(bias_yx), self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state), self._p(view.tail),
+            self._p(out), batch.num_segments, channels, blocks, view.taps, 1 if write_state else 0, self._stream()),
+            "gated_recurrence")
+        return out
+
+    # ------------------------------------------------------------------ attention with a sink, a cap, chunks
+    def qk_norm_rope_write(self, qkv, batch, q_norm, k_norm, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, view,
+                           write_kv=True):
+        """In place on qkv [T, heads * dim | kv_heads * dim | kv_heads * vdim]: RMS norm per head of q and k (weights
+        float32 [dim] or None), rotation of their first rotary_dim elements; keys and values go into their pages."""
+        tokens = qkv.shape[0]
+        if qkv.shape[1] != (heads + kv_heads) * dim + kv_heads * vdim or not qkv.is_contiguous():
+            raise KernelError("qk_norm_rope_write: qkv must be contiguous [tokens, heads * dim + kv_heads * (dim + vdim)]")
+        if (q_norm is None) != (k_norm is None):
+            raise KernelError("qk_norm_rope_write: both norms or none")
+        write = bool(write_kv and view is not None)
+        if write and (view.keys.dtype != qkv.dtype or not view.keys.is_contiguous() or not view.values.is_contiguous()):
+            raise KernelError("qk_norm_rope_write: cache pages must be contiguous and of the compute dtype")
+        self._check(self.lib.ttb_qk_norm_rope_write(
+            self._p(qkv), _dtype_code(qkv.dtype), qkv.stride(0), self._p(batch.positions), self._p(batch.seg_of_token),
+            self._p(q_norm), self._p(k_norm), ctypes.c_float(eps), self._p(inv_freq), int(rotary_dim), tokens, heads, kv_heads,
+            dim, vdim, self._p(view.keys if write else None), self._p(view.values if write else None),
+            self._p(view.block_table if write else None), view.block_table.shape[1] if write else 0,
+            view.page_size if write else 1, view.keys.shape[0] if write else 0, 1 if write else 0, self._p(self.status),
+            self._stream()), "qk_norm_rope_write")
+
+    def sink_attention(self, qkv, batch, heads, kv_heads, dim, vdim, scale, softcap, sinks, view):
+        """Causal attention of the queries in qkv over the paged keys and values, with a cap on the scores, chunks or
+        a window (from the view) and a sink per head (float32 [heads] or None). -> [T, heads * vdim]."""
+        tokens = qkv.shape[0]
+        if view.keys.dtype != qkv.dtype:
+            raise KernelError("sink_attention: cache pages and queries differ in dtype")
+        out = torch.empty(tokens, heads * vdim, dtype=qkv.dtype, device=self.device)
+        self._check(self.lib.ttb_paged_attention_generic_ext(
+            self._p(qkv), qkv.stride(0), self._p(out), _dtype_code(qkv.dtype), self._p(batch.positions),
+            self._p(batch.seg_of_token), self._p(view.keys), self._p(view.values), self._p(view.block_table),
+            view.block_table.shape[1], view.page_size, tokens, heads, kv_heads, dim, ctypes.c_float(scale),
+            int(view.window or 0), view.keys.shape[0], self._p(self.status), vdim, ctypes.c_float(softcap or 0.0),
+            int(view.chunk or 0), self._p(sinks), self._stream()), "sink_attention")
+        return out
+
+    # ------------------------------------------------------------------ experts chosen from the best groups
+    def route_grouped(self, x, w_router, experts, top, groups, keep, floor):
+        """Float32 router over all experts' softmax scores, restricted to the `keep` best of `groups` groups:
+        -> (int32 [T, top], float32 [T, top] = chosen scores / (their sum + floor))."""
+        T, width = x.shape
+        if w_router.dtype != torch.float32 or w_router.shape != (experts, width) or x.stride(1) != 1 or not w_router.is_contiguous():
+            raise KernelError("route_grouped: the router's matrix must be float32 [experts, width]")
+        choice = torch.empty(T, top, dtype=torch.int32, device=self.device)
+        weight = torch.empty(T, top, dtype=torch.float32, device=self.device)
+        self._check(self.lib.ttb_route_grouped(self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(w_router), T, width,
+                                               experts, top, groups, keep, ctypes.c_float(floor), self._p(choice),
+                                               self._p(weight), self._stream()), "route_grouped")
+        return choice, weight
+
+    def plain_experts(self, x, choice, weight, w_up, w_down, activation="relu2"):
+        """x [T, width]; choice, weight [T, top]; w_up [E, inter, width]; w_down [E, width, inter] -> float32 [T, width]:
+        sum_j weight[t, j] * W_down,e act(W_up,e x[t]), e = choice[t, j], summed in the order of j."""
+        T, width = x.shape
+        E, inter, _ = w_up.shape
+        top = choice.shape[1]
+        pairs = T * top
+        if x.dtype != w_up.dtype or x.stride(1) != 1 or not w_up.is_contiguous() or not w_down.is_contiguous():
+            raise KernelError("plain_experts: operands must share a dtype and be contiguous")
+        if activation != "relu2":
+            raise KernelError("plain_experts: relu2 is the activation that is built")
+        out = torch.empty(T, width, dtype=torch.float32, device=self.device)
+        code = _dtype_code(x.dtype)
+        if pairs <= self.MOE_GEMV_PAIRS and width * 4 <= 48 * 1024 and top * inter * 4 <= 48 * 1024:
+            hidden = torch.empty(pairs, inter, dtype=x.dtype, device=self.device)
+            self._check(self.lib.ttb_moe_gemv_plain(
+                self._p(x), x.stride(0), self._p(w_up), self._p(w_down), self._p(choice), self._p(weight), self._p(hidden),
+                self._p(out), code, T, E, top, inter, width, self._stream()), "moe_gemv_plain")
+            self.launches += 1
+            return out
+        # many pairs: the tokens' rows are laid out expert by expert; the first product leaves float32 rows in that
+        # order (the grouped products write through an index, here 0, 1, 2, ...), the activation rounds them to the
+        # compute dtype, the second product scatters to the pairs' own rows
+        offsets = torch.empty(E + 1, dtype=torch.int32, device=self.device)
+        order = torch.empty(pairs, dtype=torch.int32, device=self.device)
+        tokens_of = torch.empty(pairs, dtype=torch.int32, device=self.device)
+        straight = self._iota(pairs)
+        pre = torch.empty(pairs, inter, dtype=torch.float32, device=self.device)
+        pair_out = torch.empty(pairs, width, dtype=torch.float32, device=self.device)
+        grouped_tc = (x.dtype == torch.bfloat16 and self.use_tcgen05 is not False and pairs >= self.MOE_TCGEN05_PAIRS
+                      and width % 8 == 0 and inter % 8 == 0)
+        if grouped_tc:
+            max_tiles = -(-pairs // 128) + E
+            tile_info = torch.empty(2 * max_tiles + 1, dtype=torch.int32, device=self.device)
+            self._check(self.lib.ttb_moe_align(self._p(choice), pairs, E, top, self._p(offsets), self._p(order),
+                                               self._p(tokens_of), self._p(tile_info[1:]), self._p(tile_info), 128,
+                                               self._stream()), "moe_align")
+            grouped = self.gather_rows(x, tokens_of)
+            self._check(self.lib.ttb_moe_gemm_tcgen05(
+                self._p(grouped), width, self._p(w_up), width, self._p(pre), inter, 0, self._p(offsets), self._p(straight),
+                self._p(tile_info[1:]), self._p(tile_info), pairs, E, max_tiles, inter, width, ctypes.c_float(0.0),
+                ctypes.c_float(0.0), self._p(self.tc_error), self._stream()), "moe_up_tcgen05")
+            hidden = self.activation(pre, activation, x.dtype)
+            self._check(self.lib.ttb_moe_gemm_tcgen05(
+                self._p(hidden), inter, self._p(w_down), inter, self._p(pair_out), width, 0, self._p(offsets), self._p(order),
+                self._p(tile_info[1:]), self._p(tile_info), pairs, E, max_tiles, width, inter, ctypes.c_float(0.0),
+                ctypes.c_float(0.0), self._p(self.tc_error), self._stream()), "moe_down_tcgen05")
+        else:
+            self._check(self.lib.ttb_moe_align(self._p(choice), pairs, E, top, self._p(offsets), self._p(order),
+                                               self._p(tokens_of), None, None, 0, self._stream()), "moe_align")
+            grouped = self.gather_rows(x, tokens_of)
+            self._check(self.lib.ttb_moe_group_gemm(
+                self._p(grouped), grouped.stride(0), self._p(w_up), ctypes.c_longlong(inter * width), width, self._p(pre), inter,
+                code, 0, self._p(offsets), self._p(straight), pairs, E, top, inter, width, ctypes.c_float(0.0),
+                ctypes.c_float(0.0), self._stream()), "moe_up")
+            hidden = self.activation(pre, activation, x.dtype)
+            self._check(self.lib.ttb_moe_group_gemm(
+                self._p(hidden), inter, self._p(w_down), ctypes.c_longlong(width * inter), inter, self._p(pair_out), width,
+                code, 0, self._p(offsets), self._p(order), pairs, E, top, width, inter, ctypes.c_float(0.0),
+                ctypes.c_float(0.0), self._stream()), "moe_down")
+        self._check(self.lib.ttb_moe_combine(self._p(pair_out), self._p(weight), top, None, 0, None, self._p(out), T, width,
+                                             self._stream()), "moe_combine")
+        return out
+
+    def _iota(self, count):
+        """0, 1, .. count-1 as int32 on the device; made once and sliced (steps of a captured size never grow it)."""
+        have = getattr(self, "_iota_buffer", None)
+        if have is None or have.numel() < count:
+            have = torch.arange(max(count, 1 << 16), dtype=torch.int32, device=self.device)
+            self._iota_buffer = have
+        return have[:count]
 
     # ------------------------------------------------------------------ sampling
     def sample(self, logits, temperature=None, top_k=None, top_p=None, seeds=None, counters=None) -> torch.Tensor:

@@ -47,6 +47,8 @@ class CacheRequest:
 
     paged = True
     window = None
+    chunk = None     # a number: position i reads keys of its own chunk floor(i / chunk) only; pages wholly before
+                     # the chunk that holds a request's end are given back
 
     def storage(self, page_size: int):
         raise NotImplementedError
@@ -58,20 +60,24 @@ class CacheRequest:
 @dataclass(frozen=True)
 class PagedKV(CacheRequest):
     """Keys and values in pages. `window` None keeps all keys; a number keeps only
-    the last `window` positions readable, and pages behind it are given back."""
+    the last `window` positions readable, and pages behind it are given back. `value_dim` None: values are
+    as long as keys. `chunk`: keys are read inside the query's own chunk of that many positions only."""
 
     num_kv_heads: int
     head_dim: int
     window: Optional[int] = None
+    value_dim: Optional[int] = None
+    chunk: Optional[int] = None
     paged = True
 
     def storage(self, page_size: int):
         page = (self.num_kv_heads, page_size, self.head_dim)     # one KV head's page is contiguous
-        return {"keys": (page, None), "values": (page, None)}
+        values = (self.num_kv_heads, page_size, self.value_dim or self.head_dim)
+        return {"keys": (page, None), "values": (values, None)}
 
     def view(self, tensors, *, block_table, page_size, **_):
         return PagedKVView(keys=tensors["keys"], values=tensors["values"], block_table=block_table,
-                           page_size=page_size, window=self.window)
+                           page_size=page_size, window=self.window, chunk=self.chunk)
 
 
 @dataclass(frozen=True)
@@ -128,6 +134,34 @@ class PagedKVView:
     block_table: torch.Tensor   # int32 [segments, pages_per_request]; entry i covers positions i*page_size ..
     page_size: int
     window: Optional[int]
+    chunk: Optional[int] = None
+
+
+@dataclass(frozen=True)
+class RecurrentState(CacheRequest):
+    """What a gated linear recurrence over `channels` channels behind a short causal convolution keeps per live
+    request: the recurrence's state (float32) and the convolution's last `taps - 1` inputs (compute dtype).
+    Zeroed at admission."""
+
+    channels: int
+    taps: int
+    paged = False
+
+    def storage(self, page_size: int):
+        return {"state": ((self.channels,), torch.float32), "tail": ((max(self.taps - 1, 1), self.channels), None)}
+
+    def view(self, tensors, *, slots, slot_list, **_):
+        return RecurrentStateView(state=tensors["state"], tail=tensors["tail"], taps=self.taps, slots=slots,
+                                  slot_list=slot_list)
+
+
+@dataclass
+class RecurrentStateView:
+    state: torch.Tensor         # float32 [max_slots + 1, channels]
+    tail: torch.Tensor          # [max_slots + 1, taps - 1, channels], oldest input first
+    taps: int
+    slots: torch.Tensor         # int32 [segments] on the device
+    slot_list: List[int]
 
 
 @dataclass
@@ -212,6 +246,17 @@ class PendingDelta:
         raise NotImplementedError
 
 
+class SumDelta(PendingDelta):
+    """Several sub-layer outputs (any dtype, each [rows, width]) that join the stream together: a norm that knows
+    the kind adds them in its own kernel, everything else calls settle()."""
+
+    def __init__(self, tensors, kernels):
+        self.tensors, self.kernels = [t for t in tensors if t is not None], kernels
+
+    def settle(self, residual) -> None:
+        self.kernels.stream_add_norm(residual, self.tensors)
+
+
 class _Added:
     """What a part returns instead of its output when it has already added that output to the
     residual stream it was given."""
@@ -244,7 +289,7 @@ class Mixer(Part):
 
     forward(x [T, width], batch, cache, write_cache) -> [T, width].
     `cache` is the view that matches cache_request(): PagedKVView, SlotStateView or
-    None. With write_cache False the unit belongs to an earlier entry of the
+    None; a mixer whose cache_request() is a tuple of requests gets a tuple of views. With write_cache False the unit belongs to an earlier entry of the
     layer order and must only be read.
     """
 
@@ -318,6 +363,17 @@ class OutputHead(Part):
         raise NotImplementedError
 
 
+class StreamStep(Part):
+    """Something that happens to the residual stream between two entries of the layer order (the start of a
+    pass over looped layers, say). forward(x float32 [T, width], embedded float32 [T, width] or None, batch)
+    changes x in place; `needs_embedding` True asks the model to keep the embedding's output for it."""
+
+    needs_embedding = False
+
+    def forward(self, x, embedded, batch):
+        raise NotImplementedError
+
+
 class Block:
     """How the parts of one layer are arranged. `slots` names the parts a block kind is built from and
     the category each is looked up in; a LayerSpec gives a PartSpec for every name, the model builds
@@ -348,12 +404,13 @@ class Block:
 # ----------------------------------------------------------------------------- registries
 _REGISTRIES: Dict[str, Dict[str, Callable]] = {
     "mixer": {}, "feed_forward": {}, "norm": {}, "position": {}, "block": {}, "embedding": {}, "head": {},
+    "stream_step": {},
 }
 
 
 def register_part(category: str, kind: str, factory: Callable) -> None:
     """Make `factory(**params)` available as `kind` in `category` (mixer,
-    feed_forward, norm, position, block, embedding, head). Registering a kind again replaces it."""
+    feed_forward, norm, position, block, embedding, head, stream_step). Registering a kind again replaces it."""
     if category not in _REGISTRIES:
         raise KeyError(f"unknown part category {category!r}; known: {sorted(_REGISTRIES)}")
     _REGISTRIES[category][kind] = factory

@@ -15,7 +15,7 @@ tensors only, as before.
 
 from __future__ import annotations
 
-from .base import ADDED, Block, DeferredNorm, PendingDelta, register_part
+from .base import ADDED, Block, DeferredNorm, PendingDelta, SumDelta, register_part
 
 
 def _normed(norm, consumer, x, delta):
@@ -115,3 +115,39 @@ class SandwichMixerBlock(SandwichBlock):
 
 register_part("block", "sandwich", SandwichBlock)
 register_part("block", "sandwich_mixer_only", SandwichMixerBlock)
+
+
+class ParallelBlock(Block):
+    """One norm, and both sub-layers read its output: h = norm1(x); x += mixer(h) + ff(h). The two outputs travel
+    on as one SumDelta and are added to the float32 stream inside the next norm's kernel (the norm part must take a
+    SumDelta: kind `rmsnorm`)."""
+
+    slots = {"norm1": "norm", "mixer": "mixer", "feed_forward": "feed_forward"}
+    takes_pending = True
+
+    def __init__(self, norm1, mixer, feed_forward=None):
+        self.norm1, self.mixer, self.feed_forward = norm1, mixer, feed_forward
+
+    def forward(self, x, delta, batch, cache, write_cache=True):
+        if isinstance(delta, PendingDelta) and not isinstance(delta, SumDelta):
+            delta.settle(x)
+            delta = None
+        if delta is ADDED or isinstance(delta, DeferredNorm):
+            delta = None
+        h = self.norm1.forward_add(x, delta)
+        mixed = self.mixer.forward(h, batch, cache, write_cache)
+        fed = self.feed_forward.forward(h, batch) if self.feed_forward is not None else None
+        return x, SumDelta([mixed, fed], self.mixer.runtime.kernels)
+
+
+class ParallelMixerBlock(ParallelBlock):
+    """The same block for a layer without a feed-forward: x += mixer(norm1(x))."""
+
+    slots = {"norm1": "norm", "mixer": "mixer"}
+
+    def graph_safe(self) -> bool:
+        return bool(getattr(self.mixer, "graph_safe", False))
+
+
+register_part("block", "parallel", ParallelBlock)
+register_part("block", "parallel_mixer_only", ParallelMixerBlock)

@@ -42,3 +42,37 @@ class SwiGLU(FeedForward):
 
 
 register_part("feed_forward", "swiglu", SwiGLU)
+
+
+class GatedMLP(FeedForward):
+    """W_down (act(W_gate h) * (W_up h)) with the activation and the tensor names as parameters: `activation`
+    "silu" or "gelu_tanh" (0.5 z (1 + tanh(sqrt(2/pi) (z + 0.044715 z^3)))); `names` = (gate, up, down) after
+    `prefix`. The activation is computed in float32 on the product's output."""
+
+    graph_safe = True
+
+    def __init__(self, width: int, inter: int, prefix: str, activation: str = "silu", names=("gate", "up", "down")):
+        self.width, self.inter, self.prefix, self.activation = int(width), int(inter), prefix, activation
+        self.names = tuple(names)
+        if activation not in ("silu", "gelu_tanh"):
+            raise ValueError(f"activation {activation!r} is not known; known: ['silu', 'gelu_tanh']")
+
+    def tensor_specs(self):
+        p, (g, u, d) = self.prefix, self.names
+        return [TensorSpec(p + g, (self.inter, self.width)), TensorSpec(p + u, (self.inter, self.width)),
+                TensorSpec(p + d, (self.width, self.inter))]
+
+    def bind(self, tensors, runtime):
+        super().bind(tensors, runtime)
+        p, (g, u, d) = self.prefix, self.names
+        self.w_gate_up = runtime.matrix(torch.cat([tensors[p + g], tensors[p + u]], 0))
+        self.w_down = runtime.matrix(tensors[p + d])
+
+    def forward(self, x, batch):
+        k = self.runtime.kernels
+        if self.activation == "silu":
+            return k.linear(k.linear_swiglu(x, self.w_gate_up), self.w_down)
+        return k.linear(k.glu_activation(k.linear(x, self.w_gate_up), self.activation), self.w_down)
+
+
+register_part("feed_forward", "gated_mlp", GatedMLP)

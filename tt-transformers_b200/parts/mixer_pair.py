@@ -1,0 +1,70 @@
+"""Two mixers side by side: both read the same input, each output is RMS-normed over the model width with a
+plain weight of its own, and the result is their mean:
+
+    out = (rms(left(h)) * w_left + rms(right(h)) * w_right) / 2
+
+The two mixers are parts of any registered kind, given as PartSpecs; each keeps what it asks of the cache
+(the layer's cache unit is a tuple of theirs). The layer's position encoding goes to the mixers named in
+`positioned`.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .base import Mixer, PartSpec, TensorSpec, build_part, register_part
+
+
+class MixerPair(Mixer):
+    def __init__(self, width: int, eps: float, left: PartSpec, right: PartSpec, left_norm: str, right_norm: str,
+                 positioned=("left",), position=None):
+        self.width, self.eps = int(width), float(eps)
+        self.left_norm, self.right_norm = left_norm, right_norm
+
+        def build(name, spec):
+            if position is not None and name in positioned:
+                spec = PartSpec(spec.kind, dict(spec.params, position=position))
+            return build_part("mixer", spec)
+
+        self.left, self.right = build("left", left), build("right", right)
+        requests = [m.cache_request() for m in (self.left, self.right)]
+        self._requests = requests
+        self.graph_safe = bool(getattr(self.left, "graph_safe", False) and getattr(self.right, "graph_safe", False))
+
+    def tensor_specs(self):
+        return (self.left.tensor_specs() + self.right.tensor_specs()
+                + [TensorSpec(self.left_norm, (self.width,)), TensorSpec(self.right_norm, (self.width,))])
+
+    def bind(self, tensors, runtime):
+        super().bind(tensors, runtime)
+        self.left.bind(tensors, runtime)
+        self.right.bind(tensors, runtime)
+        f32 = dict(device=runtime.device, dtype=torch.float32)
+        self.w_left = tensors[self.left_norm].to(**f32).contiguous()
+        self.w_right = tensors[self.right_norm].to(**f32).contiguous()
+
+    def cache_request(self):
+        kept = tuple(r for r in self._requests if r is not None)
+        return kept or None
+
+    def step_tables_signature(self):
+        return ("pair",) + tuple(m.step_tables_signature() if hasattr(m, "step_tables_signature") else id(m)
+                                 for m in (self.left, self.right))
+
+    def step_tables(self, seg_lens, seg_pos0, fixed_tokens=0):
+        tables = {}
+        for m in (self.left, self.right):
+            if hasattr(m, "step_tables"):
+                tables.update(m.step_tables(seg_lens, seg_pos0, fixed_tokens))
+        return tables
+
+    def forward(self, x, batch, cache, write_cache=True):
+        views = iter(cache or ())
+        outs = []
+        for m, request in zip((self.left, self.right), self._requests):
+            view = next(views) if request is not None else None
+            outs.append(m.forward(x, batch, view, write_cache))
+        return self.runtime.kernels.mean_rmsnorm_pair(outs[0], self.w_left, outs[1], self.w_right, self.eps)
+
+
+register_part("mixer", "mixer_pair", MixerPair)

@@ -70,6 +70,8 @@ class ModelSpec:
     head: PartSpec                           # category "head"
     input_position: Optional[PartSpec] = None  # a position encoding applied to the embedded tokens
     max_positions: int = 1 << 30
+    stream_steps: tuple = ()                 # of (index into the layer order, PartSpec of category "stream_step"):
+                                             # what happens to the residual stream right before that entry runs
 
     def first_entries(self, count: int) -> "ModelSpec":
         """The same model cut to the first `count` entries of its layer order (for runs that want fewer
@@ -80,7 +82,8 @@ class ModelSpec:
         used = sorted({call.layer for call in order})
         renumber = {old: new for new, old in enumerate(used)}
         return replace(self, layers=tuple(self.layers[i] for i in used),
-                       order=tuple(LayerCall(renumber[c.layer], c.cache_of) for c in order))
+                       order=tuple(LayerCall(renumber[c.layer], c.cache_of) for c in order),
+                       stream_steps=tuple((at, spec) for at, spec in self.stream_steps if at < count))
 
 
 class DecoderModel:
@@ -113,6 +116,12 @@ class DecoderModel:
                 built[name] = build_part(category, part_spec)
             self.layers.append(factory(**built, **ls.block_params))
         self.positions = list(positions.values())
+        self.stream_steps = {}
+        for at, step_spec in spec.stream_steps:
+            if not 0 <= at < len(spec.order):
+                raise ValueError(f"a stream step is placed before layer-order entry {at}, which does not exist")
+            self.stream_steps.setdefault(at, []).append(build_part("stream_step", step_spec))
+        self._keeps_embedding = any(getattr(s, "needs_embedding", False) for ss in self.stream_steps.values() for s in ss)
         for i, call in enumerate(spec.order):
             if not 0 <= call.layer < len(self.layers):
                 raise ValueError(f"layer order entry {i} names layer {call.layer}, which does not exist")
@@ -125,6 +134,8 @@ class DecoderModel:
         if self.input_position is not None:
             parts.append(self.input_position)
         parts.extend(self.positions)
+        for steps in self.stream_steps.values():
+            parts.extend(steps)
         for block in self.layers:
             parts.extend(block.parts())
         return parts
@@ -186,10 +197,13 @@ class DecoderModel:
             x = self.input_position.embed(x, batch)
         delta = None
         order = self.spec.order
+        embedded = x.clone() if self._keeps_embedding else None
         for i, call in enumerate(order):
             owner = i if call.cache_of is None else call.cache_of
             block = self.layers[call.layer]
             view = cache.view(owner, batch)
+            for step in self.stream_steps.get(i, ()):
+                step.forward(x, embedded, batch)         # in place; commutes with a delta that is still to be added
             if isinstance(delta, PendingDelta) and not getattr(block, "takes_pending", False):
                 delta.settle(x)                   # a block kind that does not know it: plain addition first
                 delta = None

@@ -9,14 +9,19 @@ from __future__ import annotations
 
 import torch
 
-from .base import ADDED, DeferredNorm, Norm, TensorSpec, register_part
+from .base import ADDED, DeferredNorm, Norm, SumDelta, TensorSpec, register_part
 
 
 class RMSNorm(Norm):
+    """`unit_offset` True: the weight is stored around zero and the row is scaled by 1 + w."""
+
     can_defer = True
 
-    def __init__(self, width: int, eps: float, weight_name: str):
+    def __init__(self, width: int, eps: float, weight_name: str, unit_offset: bool = False):
         self.width, self.eps, self.weight_name = int(width), float(eps), weight_name
+        self.unit_offset = bool(unit_offset)
+        if self.unit_offset:
+            self.can_defer = False          # the products' fused norm epilogues know the plain weight only
 
     def tensor_specs(self):
         return [TensorSpec(self.weight_name, (self.width,))]
@@ -42,6 +47,11 @@ class RMSNorm(Norm):
             delta = None                         # prepared for another norm: the stream itself is up to date
         if delta is ADDED:
             delta = None
+        if isinstance(delta, SumDelta) or self.unit_offset or (delta is not None and delta.dtype != self.runtime.dtype):
+            # several outputs at once, outputs in another dtype than the compute dtype, or the 1 + w form
+            deltas = delta.tensors if isinstance(delta, SumDelta) else ([delta] if delta is not None else [])
+            return k.stream_add_norm(residual, deltas, weight=self.weight, eps=self.eps,
+                                     offset=1.0 if self.unit_offset else 0.0, out_dtype=self.runtime.dtype)
         return k.add_rmsnorm(residual, delta, self.weight, self.eps, self.runtime.dtype)
 
 

@@ -1,0 +1,82 @@
+"""Grouped-query attention with the options of recent decoders, each a parameter:
+
+    q, k, v = W_q h, W_k h, W_v h           (query/key size `dim`, value size `vdim`, no biases)
+    qk_norm:   q and k are RMS-normed per head over `dim` with one weight each, shared by the heads, before rotation
+    position:  the first rotary_dim elements of q and k are rotated by the token's position (pairs i, i + rotary_dim/2)
+    score = (q . k) * scale;  softcap c: score = c tanh(score / c)
+    chunk n:   position i sees j <= i with floor(i / n) = floor(j / n) only;  window w: j > i - w
+    sink:      one learned number per head joins the softmax's denominator as exp(sink_h); it has no value
+    out = W_o (heads' weighted sums of v)
+
+Keys (normed, rotated) and values go into cache pages at their positions; pages wholly before a request's
+current chunk or window are given back by the cache manager. Norms, angles, scores and softmax are float32.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .base import Mixer, PagedKV, PositionEncoding, TensorSpec, register_part
+
+
+class SinkAttention(Mixer):
+    graph_safe = True
+
+    def __init__(self, width: int, heads: int, kv_heads: int, dim: int, vdim: int, scale: float, eps: float, prefix: str,
+                 softcap: Optional[float] = None, chunk: Optional[int] = None, window: Optional[int] = None,
+                 sink: bool = False, qk_norm: bool = False, position: Optional[PositionEncoding] = None):
+        if heads % kv_heads:
+            raise ValueError(f"heads ({heads}) must be a multiple of kv_heads ({kv_heads})")
+        self.width, self.heads, self.kv_heads, self.dim, self.vdim = int(width), int(heads), int(kv_heads), int(dim), int(vdim)
+        self.scale, self.eps, self.prefix = float(scale), float(eps), prefix
+        self.softcap = None if softcap is None else float(softcap)
+        self.chunk = None if chunk is None else int(chunk)
+        self.window = None if window is None else int(window)
+        self.sink, self.qk_norm, self.position = bool(sink), bool(qk_norm), position
+        if self.softcap is not None and not self.softcap > 0:
+            raise ValueError("softcap must be positive")
+        if self.chunk is not None and self.chunk < 1:
+            raise ValueError("chunk must be positive")
+        if position is not None and getattr(position, "interleaved", False):
+            raise ValueError("neighbouring rotation pairs are not built for this mixer")
+        if position is not None and getattr(position, "rotary_dim", 0) > self.dim:
+            raise ValueError(f"the rotation covers {position.rotary_dim} elements, a head has {self.dim}")
+
+    def tensor_specs(self):
+        p, H, G = self.prefix, self.heads, self.kv_heads
+        specs = [TensorSpec(p + "q", (H * self.dim, self.width)), TensorSpec(p + "k", (G * self.dim, self.width)),
+                 TensorSpec(p + "v", (G * self.vdim, self.width)), TensorSpec(p + "o", (self.width, H * self.vdim))]
+        if self.qk_norm:
+            specs += [TensorSpec(p + "q.norm", (self.dim,)), TensorSpec(p + "k.norm", (self.dim,))]
+        if self.sink:
+            specs.append(TensorSpec(p + "sink", (H,)))
+        return specs
+
+    def bind(self, tensors, runtime):
+        super().bind(tensors, runtime)
+        p = self.prefix
+        self.w_qkv = runtime.matrix(torch.cat([tensors[p + "q"], tensors[p + "k"], tensors[p + "v"]], 0))
+        self.w_o = runtime.matrix(tensors[p + "o"])
+        f32 = dict(device=runtime.device, dtype=torch.float32)
+        self.q_norm = tensors[p + "q.norm"].to(**f32).contiguous() if self.qk_norm else None
+        self.k_norm = tensors[p + "k.norm"].to(**f32).contiguous() if self.qk_norm else None
+        self.sinks = tensors[p + "sink"].to(**f32).contiguous() if self.sink else None
+
+    def cache_request(self):
+        return PagedKV(self.kv_heads, self.dim, self.window, value_dim=self.vdim, chunk=self.chunk)
+
+    def forward(self, x, batch, cache, write_cache=True):
+        k = self.runtime.kernels
+        rotation = self.position.rotation() if self.position is not None else None
+        inv_freq, rotary_dim = rotation if rotation is not None else (None, 0)
+        qkv = k.linear(x, self.w_qkv)
+        k.qk_norm_rope_write(qkv, batch, self.q_norm, self.k_norm, self.eps, inv_freq, rotary_dim, self.heads,
+                             self.kv_heads, self.dim, self.vdim, cache, write_cache)
+        mixed = k.sink_attention(qkv, batch, self.heads, self.kv_heads, self.dim, self.vdim, self.scale, self.softcap,
+                                 self.sinks, cache)
+        return k.linear(mixed, self.w_o)
+
+
+register_part("mixer", "sink_attention", SinkAttention)
