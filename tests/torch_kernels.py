@@ -343,7 +343,7 @@ class TorchKernels:
                            write_kv=True):
         T = qkv.shape[0]
         n_qk = heads + kv_heads
-        x = qkv[:, :n_qk * dim].float().view(T, n_qk, dim)
+        x = qkv[:, :n_qk * dim].float().clone().view(T, n_qk, dim)
         if q_norm is not None:
             x = x / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + eps)
             x = torch.cat([x[:, :heads] * q_norm, x[:, heads:] * k_norm], 1)

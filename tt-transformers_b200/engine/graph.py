@@ -27,6 +27,21 @@ import torch
 OWN_ARGMAX = "own argmax"        # token_feedback value: the tokens are the argmax of this graph's replay before
 
 
+def _nobodys(engine, host, layout) -> None:
+    """Point every row of a step's packed metadata at the scratch page and the scratch slot, at position 0. A capture
+    warms the step up by running it once for real: with mixers that keep a running state per request (which a second
+    run of the same token would advance twice, unlike a key that is written to the same place twice) that run must
+    touch nobody's state. The replay that follows the capture refreshes the buffer with the step's own rows."""
+    buf, L = host.numpy(), layout
+    T, R, W = L["T"], L["R"], L["W"]
+    buf[L["o_pos"]:L["o_pos"] + T] = 0
+    buf[L["o_p0"]:L["o_p0"] + R] = 0
+    buf[L["o_slot"]:L["o_slot"] + R] = engine.cache.scratch_slot
+    for i in range(len(L["groups"])):
+        start = L["o_tab"] + i * ((R * W + 3) & ~3)
+        buf[start:start + R * W] = 0
+
+
 class DecodeGraphs:
     def __init__(self, engine):
         self._engine = weakref.ref(engine)       # no cycle with the engine: both go when the last user lets go
@@ -74,6 +89,7 @@ class DecodeGraphs:
         eng = self.engine
         W = -(-bucket // eng.cache.page_size)
         host, layout, lists = eng._fill_host(entries, pad_to=size, table_width=W, want_all=True)
+        _nobodys(eng, host, layout)
         static = torch.empty(layout["total"], dtype=torch.int32, device=eng.runtime.device)
         static.copy_(host, non_blocking=True)
         eng._record_staging()
@@ -198,6 +214,7 @@ class PromptGraphs:
     def _capture(self, size: int, entries) -> tuple:
         eng = self.engine
         host, layout, lists = self._fill(entries, size)
+        _nobodys(eng, host, layout)
         static = torch.empty(layout["total"], dtype=torch.int32, device=eng.runtime.device)
         static.copy_(host, non_blocking=True)
         eng._record_staging()
