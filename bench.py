@@ -52,7 +52,7 @@ def main(argv=None) -> int:
     parser.add_argument("--skip-e2e", action="store_true", help="leave the end-to-end measurement out (for profiling)")
     parser.add_argument("--design", default=None,
                         help="instead of the default workload: prefill and decode throughput of a named random model of "
-                             "another design (bozavik-a, bozavik-b) beside the closest dense model at equal size, with "
+                             "another design (bozavik-a, bozavik-b, pedazen-a, pedazen-b) beside the closest dense model at equal size, with "
                              "the design's own kernels against their rooflines")
     parser.add_argument("--fill", default="prefill", choices=("prefill", "synthetic"),
                         help="how the cache gets its context before decoding: through the engine's own prefill, "
@@ -73,7 +73,7 @@ def main(argv=None) -> int:
         context = min(args.context, 4096)
         result = measure.run_design_comparison(args.design, batch=args.batch, context=context,
                                                steps=min(args.steps, 32), warmup=warmup)
-        own = result["Bozavik"]
+        own = result[result["design"]]
         print(json.dumps({"metric": f"decode tokens/s, {args.design} sizes, batch {args.batch}", "value": own["decode_tokens_per_s"],
                           "unit": "tokens/s", "n_gpus": 1, "steps": min(args.steps, 32), "warmup": warmup,
                           "ms_per_step": own["decode_ms_per_step"], "higher_is_better": True, "dtype": "bf16",

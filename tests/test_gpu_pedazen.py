@@ -52,7 +52,7 @@ def _batch(segs, slots=None):
         seg_of_token=torch.cat([torch.full((n,), r) for r, n in enumerate(lens)]).to(**i32),
         cu_seqlens=torch.tensor(cu, **i32), seg_pos0=torch.tensor(pos0, **i32), seg_slot=torch.tensor(slots, **i32),
         seg_lens=lens, seg_pos0_list=pos0, seg_slot_list=slots, num_segments=len(segs), num_tokens=cu[-1],
-        max_seg_len=max(lens), max_context=max(p + n for p, n in segs))
+        max_seg_len=max(lens), max_context=max(p + n for p, n in segs), extras={})
 
 
 # ---------------------------------------------------------------------------- the stream and the norms
@@ -102,10 +102,10 @@ def test_lightning_attention_against_its_twin(kernels, twin, dtype, H, D, V):
     """Portions beside single tokens, continuing from a state that is not zero, on slots in any order; a second step
     continues from what the first left; a state that must only be read stays as it was."""
     g = torch.Generator().manual_seed(H * D + V)
-    segs = [(0, 37), (90, 1), (5, 2), (0, 1), (300, 70)]
-    slots = [3, 0, 5, 1, 4]
+    segs = [(0, 37), (90, 1), (5, 2), (0, 1), (300, 70), (0, 200)]
+    slots = [3, 0, 5, 1, 4, 6]
     decays = torch.tensor([1.0, 0.0, 0.999, 0.6, 0.9][:H] if H <= 5 else [0.9] * H, device=DEV)
-    state = (torch.randn(7, H, D, V, generator=g) * 0.5).to(DEV)
+    state = (torch.randn(8, H, D, V, generator=g) * 0.5).to(DEV)
     for step in range(2):
         batch = _batch(segs, slots)
         proj = torch.randn(batch.num_tokens, 2 * H * D + 2 * H * V + 3, generator=g).to(DEV, dtype)
@@ -114,13 +114,38 @@ def test_lightning_attention_against_its_twin(kernels, twin, dtype, H, D, V):
         v_got = SlotState((H, D, V)).view({"state": s_got}, slots=batch.seg_slot, slot_list=slots)
         ref = twin.lightning_attention(proj, batch, v_ref, H, D, V, decays)
         got = kernels.lightning_attention(proj, batch, v_got, H, D, V, decays)
-        _close(got, ref, 5e-5 if dtype == torch.float32 else 1e-4)        # the same rounded inputs, float32 arithmetic
-        _close(s_got, s_ref, 5e-5 if dtype == torch.float32 else 1e-4)
-        assert torch.equal(s_got[[2, 6]], state[[2, 6]])                   # nobody's slots are nobody's
+        # float32 arithmetic on the same inputs; the chunked form rounds the activations to bfloat16 first
+        _close(got, ref, 5e-5 if dtype == torch.float32 else 1e-2)
+        _close(s_got, s_ref, 5e-5 if dtype == torch.float32 else 1e-2)
+        assert torch.equal(s_got[[2, 7]], state[[2, 7]])                   # nobody's slots are nobody's
         kept = s_got.clone()
         kernels.lightning_attention(proj, batch, v_got, H, D, V, decays, write_state=False)
         assert torch.equal(s_got, kept)
         state = s_got
+
+
+@pytest.mark.parametrize("H,D,V", [(2, 128, 64), (3, 48, 20), (1, 16, 40), (2, 256, 32)])
+def test_lightning_chunks_keep_float32_where_the_recurrence_does(kernels, H, D, V):
+    """Pre-activations from 20 on are their own silu in float32 and exact in bfloat16, so nothing but the arithmetic
+    differs between the chunked form and the walk token by token: decays, state and weights must agree to float32
+    rounding and the two-halves splitting (2^-17), not to bfloat16's."""
+    g = torch.Generator().manual_seed(D + V)
+    segs, slots = [(0, 150), (40, 17), (3, 64), (9, 65)], [2, 0, 1, 3]
+    decays = torch.tensor([0.999, 0.9, 0.6][:H], device=DEV)
+    batch = _batch(segs, slots)
+    proj = torch.randint(20, 29, (batch.num_tokens, 2 * H * D + 2 * H * V), generator=g).to(DEV, torch.bfloat16)
+    state = (torch.randn(4, H, D, V, generator=g) * 1e4).to(DEV)
+    results = []
+    for chunks in (True, False):
+        kernels.use_lightning_chunks = chunks
+        try:
+            s_now = state.clone()
+            view = SlotState((H, D, V)).view({"state": s_now}, slots=batch.seg_slot, slot_list=slots)
+            results.append((kernels.lightning_attention(proj, batch, view, H, D, V, decays), s_now))
+        finally:
+            kernels.use_lightning_chunks = True
+    _close(results[0][0], results[1][0], 3e-5)
+    _close(results[0][1], results[1][1], 3e-5)
 
 
 # ---------------------------------------------------------------------------- the recurrent block
@@ -129,12 +154,12 @@ def test_lightning_attention_against_its_twin(kernels, twin, dtype, H, D, V):
 def test_convolution_and_recurrence_against_their_twins(kernels, twin, dtype, C, B, taps):
     """Portions shorter and longer than the convolution's reach, single tokens, first tokens; two steps in a row."""
     g = torch.Generator().manual_seed(C + taps)
-    segs = [(0, 23), (40, 1), (7, 2), (0, 1), (11, 3), (64, 50)]
-    slots = [2, 0, 5, 1, 6, 3]
+    segs = [(0, 23), (40, 1), (7, 2), (0, 1), (11, 3), (64, 50), (9, 300)]
+    slots = [2, 0, 5, 1, 6, 3, 7]
     s = C // B
     req = RecurrentState(C, taps)
-    state = torch.randn(8, C, generator=g).to(DEV)
-    tail = torch.randn(8, max(taps - 1, 1), C, generator=g).to(DEV, dtype)
+    state = torch.randn(9, C, generator=g).to(DEV)
+    tail = torch.randn(9, max(taps - 1, 1), C, generator=g).to(DEV, dtype)
     conv_w, conv_b = (torch.randn(C, taps, generator=g) * 0.5).to(DEV), (torch.randn(C, generator=g) * 0.3).to(DEV)
     b_in = (torch.randn(2 * C, generator=g) * 0.3).to(DEV)
     w_gates = (torch.randn(B, 2 * s, s, generator=g) * s ** -0.5).to(DEV, dtype)
@@ -158,7 +183,7 @@ def test_convolution_and_recurrence_against_their_twins(kernels, twin, dtype, C,
         _close(st_got, st_ref, 2e-5)
         if taps > 1:
             _close(tl_got, tl_ref, 1e-6)
-        assert torch.equal(st_got[[4, 7]], state[[4, 7]])
+        assert torch.equal(st_got[[4, 8]], state[[4, 8]])
         state, tail = st_got, tl_got
 
 
@@ -190,7 +215,8 @@ def _attention_setup(segs, heads, kv_heads, dim, vdim, page, chunk, window, dtyp
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("heads,kv_heads,dim,vdim,rot,page,chunk,window", [
     (8, 8, 96, 96, 48, 16, 96, None), (4, 2, 32, 16, 16, 4, 24, None), (1, 1, 10, 7, 6, 8, 7, None), (5, 5, 6, 9, 2, 16, 1, None),
-    (6, 1, 16, 48, 16, 16, 16, None), (3, 1, 64, 128, 0, 32, None, None), (2, 2, 24, 40, 24, 16, 50, 20), (4, 4, 136, 520, 8, 16, None, 33)])
+    (6, 1, 16, 48, 16, 16, 16, None), (3, 1, 64, 128, 0, 32, None, None), (2, 2, 24, 40, 24, 16, 50, 20), (4, 4, 136, 264, 8, 16, None, 33),
+    (8, 2, 64, 64, 32, 16, 96, None), (4, 1, 128, 128, 128, 16, None, 100), (6, 3, 64, 64, 0, 32, 200, None), (2, 2, 128, 128, 64, 8, 33, None)])
 def test_sink_attention_against_its_twin(kernels, twin, dtype, heads, kv_heads, dim, vdim, rot, page, chunk, window):
     segs = [(0, 70), (129, 1), (63, 2), (64, 1), (0, 1), (300, 1), (127, 3), (page - 1, 2), (15, 40), (95, 3), (96, 1)]
     batch, view, qkv, g = _attention_setup(segs, heads, kv_heads, dim, vdim, page, chunk, window, dtype, seed=heads * dim + vdim)
@@ -276,7 +302,14 @@ def test_engine_matches_the_plain_implementation(tmp_path, dtype, tol, name):
             engine.cache.audit()
             assert engine.cache.free_pages() == pages and engine.cache.free_slots == 4
             for rid in ref:
-                assert helpers.relative_error(got[rid], ref[rid]) < tol, (make_steps.__name__, graphs, rid)
+                if dtype == "float32":
+                    assert helpers.relative_error(got[rid], ref[rid]) < tol, (make_steps.__name__, graphs, rid)
+                else:
+                    # in bfloat16 a router's close call may go the other way for a token or two: nine rows in ten
+                    # must agree, and the typical row closely
+                    scale = float(ref[rid].abs().max())
+                    rows = (got[rid] - ref[rid]).abs().amax(dim=-1) / scale
+                    assert float((rows < tol).float().mean()) >= 0.9 and float(rows.median()) < tol / 2, (make_steps.__name__, graphs, rid)
             engine.close()
 
 

@@ -47,10 +47,50 @@ def bozavik_config(width, layers, heads, dim, rot_dim, vdim, q_rank, kv_rank, ex
                         "mlp": mlp} for i in range(layers)]}
 
 
+def pedazen_config(width, pairs, lightning_heads, heads, kv_heads, head_dim, chunk, channels, blocks, experts, top, ff, groups,
+                   keep, dense_ff, vocab, loop=None):
+    """`pairs` times a linear-attention layer followed by a layer with softmax attention and a recurrent block side
+    by side; the first layer has a dense feed-forward, the others routed experts."""
+    def lightning():
+        decay = [1.0 - 2.0 ** (-3 - 5 * h / max(1, lightning_heads - 1)) for h in range(lightning_heads)]
+        return {"type": "lightning", "mixer": {"heads": lightning_heads, "dim": head_dim, "vdim": head_dim, "decay": decay}}
+
+    def parallel():
+        left = {"heads": heads, "kv_heads": kv_heads, "dim": head_dim, "vdim": head_dim, "mask": {"size": chunk},
+                "rot": {"base": 10000.0, "dims": head_dim // 2}, "scale": head_dim ** -0.5, "softcap": 30.0}
+        return {"type": "parallel", "mixer": {"left": left, "right": {"width": channels, "blocks": blocks, "conv": 4}}}
+
+    moe = {"kind": "moe", "expert": {"ff": ff}, "router": {"experts": experts, "top": top, "groups": {"count": groups, "keep": keep}}}
+    layers = []
+    for i in range(pairs):
+        layers.append(dict(lightning(), mlp={"kind": "dense", "ff": dense_ff} if i == 0 else moe))
+        layers.append(dict(parallel(), mlp=moe))
+    cfg = {"architecture": "Pedazen", "vocab": vocab, "width": width, "norm": {"eps": 1e-6}, "embedding": {"scale": 1.0},
+           "layers": layers}
+    if loop:
+        cfg["loop"] = {"start": loop[0], "stop": loop[1], "times": loop[2]}
+    return cfg
+
+
+def layer_runs(cfg: dict) -> int:
+    """How many layers a token passes in a Pedazen configuration, looped layers counted every time."""
+    loop = cfg.get("loop")
+    return len(cfg["layers"]) + ((loop["stop"] - loop["start"]) * (loop["times"] - 1) if loop else 0)
+
+
 def closest_llama(cfg: dict) -> dict:
-    """The dense decoder of this package that is closest to a Bozavik configuration: the same width, depth,
-    vocabulary and heads (head size = unrotated + rotated query elements), one KV head per four heads, and a
-    feed-forward as wide as the experts a token uses plus the shared one."""
+    """The dense decoder of this package that is closest to a configuration of another design: the same width,
+    depth and vocabulary. For Bozavik: the same heads (head size = unrotated + rotated query elements), one KV
+    head per four heads, and a feed-forward as wide as the experts a token uses plus the shared one. For Pedazen:
+    as many layers as a token passes, the heads, KV heads and head size of its softmax attention, and a
+    feed-forward as wide as the experts a token uses."""
+    if cfg.get("architecture") == "Pedazen":
+        left = next(l["mixer"]["left"] for l in cfg["layers"] if l["type"] == "parallel")
+        f = next(l["mlp"] for l in cfg["layers"] if l["mlp"] and l["mlp"]["kind"] == "moe")
+        return {"architectures": ["LlamaForCausalLM"], "hidden_size": cfg["width"], "num_hidden_layers": layer_runs(cfg),
+                "num_attention_heads": left["heads"], "num_key_value_heads": left["kv_heads"], "head_dim": left["dim"],
+                "intermediate_size": f["router"]["top"] * f["expert"]["ff"], "vocab_size": cfg["vocab"], "rms_norm_eps": 1e-5,
+                "max_position_embeddings": 131072, "rope_theta": 500000.0, "tie_word_embeddings": True}
     layer = cfg["layers"][-1]
     m, f = layer["mixer"], layer["mlp"]
     heads, head_dim = m["heads"], m["dim"] + m.get("rot_dim", 0)
@@ -65,6 +105,13 @@ RANDOM_MODELS.update({
     "bozavik-tiny": bozavik_config(128, 2, 4, 16, 16, 16, 64, 64, 4, 2, 64, 64, 512),
     "bozavik-a": bozavik_config(1024, 8, 16, 32, 32, 64, 384, 128, 16, 4, 512, 1024, 32768),
     "bozavik-b": bozavik_config(2048, 8, 16, 64, 64, 128, 768, 256, 32, 4, 1024, 2048, 65536),
+})
+
+
+RANDOM_MODELS.update({
+    "pedazen-tiny": pedazen_config(128, 1, 2, 4, 2, 64, 64, 128, 2, 4, 2, 64, 2, 1, 256, 512, loop=(0, 2, 2)),
+    "pedazen-a": pedazen_config(1024, 4, 8, 16, 4, 64, 1024, 1024, 8, 16, 4, 512, 4, 2, 2048, 32768, loop=(2, 4, 2)),
+    "pedazen-b": pedazen_config(2048, 4, 16, 16, 4, 128, 2048, 2048, 8, 32, 4, 1024, 8, 4, 4096, 65536, loop=(2, 4, 2)),
 })
 
 

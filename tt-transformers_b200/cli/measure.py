@@ -547,6 +547,9 @@ class KernelTimer:
 
 _TIMED = {"Bozavik": ["add_layernorm", "latent_prepare", "heads_linear", "_latent_attention", "latent_out", "gate_heads", "route_top",
                       "routed_experts", "linear"],
+          "Pedazen": ["stream_add_norm", "lightning_attention", "gated_rmsnorm", "qk_norm_rope_write", "sink_attention",
+                      "causal_conv", "heads_linear", "gated_recurrence", "mean_rmsnorm_pair", "route_grouped", "plain_experts",
+                      "glu_activation", "linear"],
           "Llama": ["add_rmsnorm", "rope_kv_write", "fused_qkv_rope", "paged_attention", "linear_swiglu", "linear"]}
 
 
@@ -576,6 +579,41 @@ def _kernel_work(cfg: dict, tokens: int, contexts: List[int], new_per_request: i
                 sff = (f.get("shared") or {}).get("ff", 0)          # the shared expert runs inside the same call
                 add("routed_experts", 2 * tokens * 3 * (top * ff + sff) * width,
                     2 * (used * ff + sff) * 3 * width + tokens * width * (2 + 4))
+    elif cfg.get("architecture") == "Pedazen":
+        width = cfg["width"]
+        loop = cfg.get("loop")
+        runs = [1 + ((loop["times"] - 1) if loop and loop["start"] <= i < loop["stop"] else 0) for i in range(len(cfg["layers"]))]
+        for layer, times in zip(cfg["layers"], runs):
+            m, f = layer["mixer"], layer["mlp"]
+            for _ in range(times):
+                add("stream_add_norm", 0, tokens * width * (4 + 4 + 4 + 4 + 2))            # stream in and out, two outputs in, h out
+                if layer["type"] == "lightning":
+                    H, D, V = m["heads"], m["dim"], m["vdim"]
+                    # the recurrence costs 4 D V flops a token and head however it is cut; q, k, v in, o out, the state in and out
+                    add("lightning_attention", 4.0 * tokens * H * D * V,
+                        tokens * H * ((2 * D + V) * 2 + V * 4) + 2 * len(contexts) * H * D * V * 4)
+                    add("gated_rmsnorm", 0, tokens * H * V * (4 + 2 + 2))
+                else:
+                    a, r = m["left"], m["right"]
+                    H, G, D, V, C = a["heads"], a["kv_heads"], a["dim"], a["vdim"], r["width"]
+                    n = a["mask"]["size"]
+                    seen = []                                   # keys that the step's queries see, summed over the queries
+                    for ctx in contexts:
+                        for pos in range(ctx - new_per_request, ctx):
+                            seen.append(pos % n + 1)
+                    keys_read = sum(min(ctx, max(seen[i * new_per_request:(i + 1) * new_per_request]) + new_per_request)
+                                    for i, ctx in enumerate(contexts))
+                    add("sink_attention", 2.0 * H * sum(seen) * (D + V), 2 * (keys_read * G * (D + V) + tokens * H * (D + V)))
+                    add("qk_norm_rope_write", 0, tokens * ((H + G) * D * 2 * 2 + G * (D + V) * 2 + G * V * 2))
+                    add("causal_conv", 0, tokens * C * 2 * 2)
+                    add("gated_recurrence", 0, tokens * C * (8 + 2 + 2 + 2))
+                    add("heads_linear", 2.0 * tokens * 2 * C * (C // r["blocks"]), tokens * C * (2 + 8) + 2 * C * (C // r["blocks"]) * 2)
+                    add("mean_rmsnorm_pair", 0, tokens * width * (2 + 2 + 4))
+                if f and f["kind"] == "moe":
+                    top, ff, experts = f["router"]["top"], f["expert"]["ff"], f["router"]["experts"]
+                    used = min(experts, tokens * top)
+                    add("plain_experts", 2.0 * tokens * 2 * top * ff * width, 2 * used * ff * 2 * width + tokens * width * (2 + 4))
+                    add("route_grouped", 2.0 * tokens * experts * width, tokens * width * 2 + experts * width * 4)
     else:
         width, heads, kv, hd = cfg["hidden_size"], cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
         for _ in range(cfg["num_hidden_layers"]):
@@ -606,16 +644,21 @@ def _step_kernel_times(engine, family: str, entries_fn, reps: int = 3) -> Dict[s
 
 def run_design_comparison(name: str = "bozavik-a", *, prefill_tokens: int = PREFILL_TOKENS, batch: int = 8,
                           context: int = 4096, steps: int = 32, warmup: int = 4, device: str = "cuda:0") -> dict:
-    """Prefill and decode throughput of a named Bozavik model (random weights) and of the dense decoder closest to
-    it at equal size, and, kernel by kernel, how far the design's own kernels are from their rooflines beside the
-    like kernels of the dense model (eager steps, CUDA events around each kernel-table call)."""
+    """Prefill and decode throughput of a named model of another design (Bozavik, Pedazen; random weights) and of the
+    dense decoder closest to it at equal size, and, kernel by kernel, how far the design's own kernels are from their
+    rooflines beside the like kernels of the dense model (eager steps, CUDA events around each kernel-table call)."""
     from ..engine.step import StepEntry
     from .common import closest_llama
 
     pk = peaks()
     out = {"model": name, "peaks": pk["source"], "prefill_tokens": prefill_tokens, "decode": {"batch": batch, "context": context}}
-    configs = {"Bozavik": dict(RANDOM_MODELS[name])}
-    configs["Llama"] = closest_llama(configs["Bozavik"])
+    design = RANDOM_MODELS[name].get("architecture")
+    if design not in _TIMED:
+        raise SystemExit(f"{name!r} is no model of another design; known: "
+                         f"{sorted(n for n, c in RANDOM_MODELS.items() if c.get('architecture') in _TIMED)}")
+    out["design"] = design
+    configs = {design: dict(RANDOM_MODELS[name])}
+    configs["Llama"] = closest_llama(configs[design])
     for family, cfg in configs.items():
         vocab = cfg.get("vocab", cfg.get("vocab_size"))
         prompts = Prompts(vocab)

@@ -67,7 +67,11 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
                      const int* __restrict__ qtile_seg, const int* __restrict__ qtile_tok0,
                      int heads, int kv_heads, float scale_log2, int window, int num_splits,
                      float* __restrict__ partial_o, float* __restrict__ partial_ml, int num_pages,
-                     int* __restrict__ status) {
+                     int* __restrict__ status, float softcap, float softcap_scale, int chunk_size,
+                     const float* __restrict__ sinks) {
+    // Options, all off at zero / null: softcap c: score = c * tanh(q.k * softcap_scale) with softcap_scale = scale / c
+    // (scale_log2 is then log2(e) alone); chunk_size n: position p sees the keys from floor(p / n) * n on only;
+    // sinks: one more term 2^(sink_h * log2(e)) of every row's denominator, with no value (it joins in split 0).
     constexpr int BM = 16 * WM;
     constexpr int THREADS = WM * WN * 32;
     constexpr int CHUNKS = HD / 8;              // 16-byte chunks per row
@@ -100,7 +104,8 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
     const int tile_tokens = min(tokens_per_tile, seg_tokens - tok0);
     const int valid_rows = tile_tokens * rep;
     const int q_first = pos0 + tok0, q_last = q_first + tile_tokens - 1;
-    const int lo = (window > 0 && q_first - window + 1 > 0) ? q_first - window + 1 : 0;
+    int lo = (window > 0 && q_first - window + 1 > 0) ? q_first - window + 1 : 0;
+    if (chunk_size > 0 && q_first / chunk_size * chunk_size > lo) lo = q_first / chunk_size * chunk_size;
     const int total = q_last - lo + 1;
     const int chunk = ((total + num_splits - 1) / num_splits + AM_BN - 1) / AM_BN * AM_BN;
     const int k_begin = lo + split * chunk;
@@ -213,9 +218,16 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
             // ---- mask (only in tiles that the causal edge, a window or the end of the range cuts),
             //      running maximum and sum. Scores stay unscaled; the scale goes into the exponent's
             //      multiply-add: p = 2^(s * scale_log2 - max * scale_log2).
+            if (softcap > 0.f) {
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) s[nb][j] = softcap * tanhf(s[nb][j] * softcap_scale);
+            }
             const int last_key = key_base + WARP_KEYS - 1;
             const bool cut = last_key > warp_qpos_min || last_key >= k_end ||
-                             (window > 0 && key_base <= warp_qpos_max - window);
+                             (window > 0 && key_base <= warp_qpos_max - window) ||
+                             (chunk_size > 0 && key_base < warp_qpos_max / chunk_size * chunk_size);
             float tile_max[2] = {-INFINITY, -INFINITY};
             if (cut) {
 #pragma unroll
@@ -224,7 +236,8 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
                     for (int j = 0; j < 4; ++j) {
                         const int key = key_base + nb * 8 + ((lane & 3) << 1) + (j & 1);
                         const int qpos = (j < 2) ? qpos0 : qpos1;
-                        const bool visible = key < k_end && key <= qpos && (window <= 0 || key > qpos - window);
+                        const bool visible = key < k_end && key <= qpos && (window <= 0 || key > qpos - window) &&
+                                             (chunk_size <= 0 || key >= qpos / chunk_size * chunk_size);
                         if (!visible) s[nb][j] = -INFINITY;
                     }
                 }
@@ -334,6 +347,13 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
             }
             if (r >= valid_rows) continue;
             const int token = tok0 + r / rep, head = g * rep + r % rep;
+            if (sinks != nullptr && split == 0) {
+                const float sk = sinks[head] * 1.4426950408889634f, top = fmaxf(m, sk);
+                const float f = (m == -INFINITY) ? 0.f : exp2f(m - top);
+                sum = sum * f + exp2f(sk - top);
+                o *= f;
+                m = top;
+            }
             if (num_splits > 1) {
                 const size_t slot = ((size_t)(seg_start + token) * heads + head) * num_splits + split;
                 partial_o[slot * HD + c] = o;
@@ -350,6 +370,17 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
         if (r >= valid_rows) continue;
         const int token = tok0 + r / rep, head = g * rep + r % rep;
         const size_t row_index = (size_t)(seg_start + token) * heads + head;
+        if (sinks != nullptr && split == 0) {
+            const float sk = sinks[head] * 1.4426950408889634f, top = fmaxf(row_max[h], sk);
+            const float f = (row_max[h] == -INFINITY) ? 0.f : exp2f(row_max[h] - top);
+            row_sum[h] = row_sum[h] * f + exp2f(sk - top);
+            row_max[h] = top;
+#pragma unroll
+            for (int ob = 0; ob < OB; ++ob) {
+                o_acc[ob][2 * h] *= f;
+                o_acc[ob][2 * h + 1] *= f;
+            }
+        }
         if (num_splits > 1) {
             const size_t slot = row_index * num_splits + split;
 #pragma unroll
@@ -425,7 +456,8 @@ static int launch_attention(const void* qkv, int q_row_stride, void* out, const 
                             const void* key_pages, const void* value_pages, const int* block_table, int table_width,
                             int page_size, const int* qtile_seg, const int* qtile_tok0, int n_qtiles, int tokens,
                             int heads, int kv_heads, float scale, int window, int num_splits, float* partial_o,
-                            float* partial_ml, int num_pages, int* status, cudaStream_t stream) {
+                            float* partial_ml, int num_pages, int* status, float softcap, int chunk_size, const float* sinks,
+                            cudaStream_t stream) {
     constexpr int BM = 16 * WM;
     const size_t stage_bytes = (size_t)BM * HD * 2 + 2 * (size_t)STAGES * AM_BN * HD * 2 + AM_TABLE_CACHE * sizeof(int);
     const size_t merge_bytes = (size_t)BM * HD * 2 + (size_t)WN * 16 * (HD + 2) * sizeof(float);
@@ -441,12 +473,13 @@ static int launch_attention(const void* qkv, int q_row_stride, void* out, const 
         configured.mark();
     }
     dim3 grid(n_qtiles, kv_heads, num_splits);
-    const float scale_log2 = scale * 1.4426950408889634f;
+    const float scale_log2 = (softcap > 0.f ? 1.f : scale) * 1.4426950408889634f;
+    const float softcap_scale = softcap > 0.f ? scale / softcap : 0.f;
     ttb_launch(kernel, grid, dim3(WM * WN * 32), smem, stream,
         (const __nv_bfloat16*)qkv, q_row_stride, (__nv_bfloat16*)out, cu_seqlens, seg_pos0,
         (const __nv_bfloat16*)key_pages, (const __nv_bfloat16*)value_pages, block_table, table_width, page_size,
         page_shift, qtile_seg, qtile_tok0, heads, kv_heads, scale_log2, window, num_splits, partial_o, partial_ml,
-        num_pages, status);
+        num_pages, status, softcap, softcap_scale, chunk_size, sinks);
     int launch = ttb_launch_status();
     if (launch != TTB_OK || num_splits == 1) return launch;
     const int rows = tokens * heads;
@@ -499,8 +532,9 @@ static int paged_attention_mma_impl(const void* qkv, int q_row_stride, void* out
                                     const int* qtile_tok0, int n_qtiles, int tokens, int heads, int kv_heads,
                                     int head_dim, float scale, int window, int decode_shape, int num_splits,
                                     float* partial_o, float* partial_ml, int num_pages, int* status,
-                                    cudaStream_t stream) {
+                                    cudaStream_t stream, float softcap = 0.f, int chunk_size = 0, const float* sinks = nullptr) {
     if (n_qtiles == 0 || tokens == 0) return TTB_OK;
+    if (softcap < 0.f || chunk_size < 0) return TTB_ERR_ARGUMENT;
     if (!qkv || !out || !cu_seqlens || !seg_pos0 || !key_pages || !value_pages || !block_table) return TTB_ERR_ARGUMENT;
     if (!ttb_attention_mma_supports(heads, kv_heads, head_dim)) return TTB_ERR_UNSUPPORTED;
     if (num_splits < 1 || num_splits > 65535 || kv_heads > 65535) return TTB_ERR_UNSUPPORTED;
@@ -510,7 +544,7 @@ static int paged_attention_mma_impl(const void* qkv, int q_row_stride, void* out
     if (decode_shape && heads / kv_heads > 16) return TTB_ERR_UNSUPPORTED;
 #define AM_ARGS qkv, q_row_stride, out, cu_seqlens, seg_pos0, key_pages, value_pages, block_table, table_width, page_size, \
                 qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads, scale, window, num_splits, partial_o, partial_ml, \
-                num_pages, status, stream
+                num_pages, status, softcap, chunk_size, sinks, stream
     if (head_dim == 64) return decode_shape ? launch_attention<64, 1, 4, 4>(AM_ARGS) : launch_attention<64, 4, 1, 3>(AM_ARGS);
     return decode_shape ? launch_attention<128, 1, 4, 3>(AM_ARGS) : launch_attention<128, 4, 1, 2>(AM_ARGS);
 #undef AM_ARGS
@@ -540,6 +574,21 @@ TTB_EXPORT int ttb_paged_attention_mma_checked(const void* qkv, int q_row_stride
                                     table_width, page_size, qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads,
                                     head_dim, scale, window, decode_shape, num_splits, partial_o, partial_ml,
                                     num_pages, status, stream);
+}
+
+// The same with a cap on the scores (0: none), chunks (0: none) and a sink per head (null: none); see the kernel.
+TTB_EXPORT int ttb_paged_attention_mma_ext(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens,
+                                           const int* seg_pos0, const void* key_pages, const void* value_pages,
+                                           const int* block_table, int table_width, int page_size,
+                                           const int* qtile_seg, const int* qtile_tok0, int n_qtiles, int tokens,
+                                           int heads, int kv_heads, int head_dim, float scale, int window,
+                                           int decode_shape, int num_splits, float* partial_o, float* partial_ml,
+                                           int num_pages, int* status, float softcap, int chunk_size, const float* sinks,
+                                           cudaStream_t stream) {
+    return paged_attention_mma_impl(qkv, q_row_stride, out, cu_seqlens, seg_pos0, key_pages, value_pages, block_table,
+                                    table_width, page_size, qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads,
+                                    head_dim, scale, window, decode_shape, num_splits, partial_o, partial_ml,
+                                    num_pages, status, stream, softcap, chunk_size, sinks);
 }
 
 // ---------------------------------------------------------------------------------------------

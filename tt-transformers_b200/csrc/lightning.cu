@@ -103,3 +103,232 @@ TTB_EXPORT int ttb_lightning_scan(const void* proj, int dtype, int ld, const int
 #undef LS_LAUNCH
     return ttb_launch_status();
 }
+
+// ---------------------------------------------------------------- prompt portions: the same recurrence, chunk by chunk
+// For a chunk of C tokens that starts from the state S0 (L = decay):
+//   o_i   = L^(i+1) S0^T q_i + sum_(j<=i) L^(i-j) (q_i . k_j) v_j
+//   S_new = L^C S0 + sum_j L^(C-1-j) k_j v_j^T
+// which is four small matrix products per chunk on the tensor cores (bfloat16 operands, float32 sums):
+// A = Q K^T, Q S0, A' V and K^T V'. q, k and v are the activations rounded to bfloat16, as they leave the projection.
+// Everything that carries a decay or the state is float32 and enters its product as a sum of two bfloat16 numbers
+// (v = hi + lo with hi = bf16(v), lo = bf16(v - hi): sixteen bits of mantissa, 2^-17 relative), each half with a
+// product of its own: A' = A * L^(i-j), V' = V * L^(C-1-j) and S0. The state itself stays float32 in shared memory
+// for the whole segment. A block owns LC_VS columns of one head's state of one segment and walks its chunks in order.
+#include <mma.h>
+using namespace nvcuda;
+
+#define LC_C 64
+#define LC_VS 32
+#define LC_THREADS 256
+
+struct LcLayout {
+    int ldq, ldv, lda_f, lda_h, lds_f, lds_h, ldo;
+    size_t q, k, v, vh, vl, af, ah, al, sf, sh, sl, of, pw, total;
+};
+
+static __host__ __device__ inline LcLayout lc_layout(int dim) {
+    LcLayout L;
+    L.ldq = dim + 8; L.ldv = LC_VS + 8; L.lda_f = LC_C + 4; L.lda_h = LC_C + 8; L.lds_f = LC_VS + 4; L.lds_h = LC_VS + 8;
+    L.ldo = LC_VS + 4;
+    size_t at = 0;
+    L.q = at; at += (size_t)LC_C * L.ldq * 2;
+    L.k = at; at += (size_t)LC_C * L.ldq * 2;
+    L.v = at; at += (size_t)LC_C * L.ldv * 2;
+    L.vh = at; at += (size_t)LC_C * L.ldv * 2;
+    L.vl = at; at += (size_t)LC_C * L.ldv * 2;
+    L.af = at; at += (size_t)LC_C * L.lda_f * 4;
+    L.ah = at; at += (size_t)LC_C * L.lda_h * 2;
+    L.al = at; at += (size_t)LC_C * L.lda_h * 2;
+    L.sf = at; at += (size_t)dim * L.lds_f * 4;
+    L.sh = at; at += (size_t)dim * L.lds_h * 2;
+    L.sl = at; at += (size_t)dim * L.lds_h * 2;
+    L.of = at; at += (size_t)LC_C * L.ldo * 4;
+    L.pw = at; at += (size_t)(LC_C + 4) * 4;
+    L.total = at;
+    return L;
+}
+
+__device__ __forceinline__ void lc_split(float v, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+    hi = __float2bfloat16_rn(v);
+    lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+}
+
+__global__ void __launch_bounds__(LC_THREADS)
+lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int* __restrict__ cu_seqlens,
+                       const int* __restrict__ seg_slot, float* __restrict__ state, const float* __restrict__ decay,
+                       float* __restrict__ out, int heads, int dim, int vdim, int write_state) {
+    extern __shared__ __align__(128) unsigned char lc_smem[];
+    const LcLayout L = lc_layout(dim);
+    __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(lc_smem + L.q);
+    __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(lc_smem + L.k);
+    __nv_bfloat16* Vs = reinterpret_cast<__nv_bfloat16*>(lc_smem + L.v);
+    __nv_bfloat16* Vh = reinterpret_cast<__nv_bfloat16*>(lc_smem + L.vh);
+    __nv_bfloat16* Vl = reinterpret_cast<__nv_bfloat16*>(lc_smem + L.vl);
+    float* Af = reinterpret_cast<float*>(lc_smem + L.af);
+    __nv_bfloat16* Ah = reinterpret_cast<__nv_bfloat16*>(lc_smem + L.ah);
+    __nv_bfloat16* Al = reinterpret_cast<__nv_bfloat16*>(lc_smem + L.al);
+    float* Sf = reinterpret_cast<float*>(lc_smem + L.sf);
+    __nv_bfloat16* Sh = reinterpret_cast<__nv_bfloat16*>(lc_smem + L.sh);
+    __nv_bfloat16* Sl = reinterpret_cast<__nv_bfloat16*>(lc_smem + L.sl);
+    float* Of = reinterpret_cast<float*>(lc_smem + L.of);
+    float* pw = reinterpret_cast<float*>(lc_smem + L.pw);           // pw[x] = decay^x, x = 0 .. LC_C
+
+    pdl_wait();
+    pdl_launch_dependents();
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int seg = blockIdx.z, head = blockIdx.y, c0 = blockIdx.x * LC_VS;
+    const int t_begin = cu_seqlens[seg], t_end = cu_seqlens[seg + 1];
+    if (t_begin >= t_end) return;
+    float* S = state + (((size_t)seg_slot[seg] * heads + head) * dim) * vdim;
+    const float lambda = decay[head];
+    for (int x = tid; x <= LC_C; x += LC_THREADS) pw[x] = x == 0 ? 1.f : powf(lambda, (float)x);
+    for (int idx = tid; idx < dim * LC_VS; idx += LC_THREADS) {
+        const int d = idx / LC_VS, c = idx % LC_VS;
+        Sf[d * L.lds_f + c] = c0 + c < vdim ? S[(size_t)d * vdim + c0 + c] : 0.f;
+    }
+    const int q_off = head * dim, k_off = heads * dim + head * dim, v_off = 2 * heads * dim + head * vdim + c0;
+    const int d_tiles = dim / 16;
+    __syncthreads();
+
+    for (int chunk0 = t_begin; chunk0 < t_end; chunk0 += LC_C) {
+        const int n = min(LC_C, t_end - chunk0);
+        // ---- the chunk's activations, rounded to bfloat16; rows past the chunk's end are zero; the state in two halves
+        for (int idx = tid; idx < LC_C * dim; idx += LC_THREADS) {
+            const int i = idx / dim, d = idx % dim;
+            float q = 0.f, k = 0.f;
+            if (i < n) {
+                const __nv_bfloat16* row = proj + (size_t)(chunk0 + i) * ld;
+                q = ls_silu(__bfloat162float(row[q_off + d]));
+                k = ls_silu(__bfloat162float(row[k_off + d]));
+            }
+            Qs[i * L.ldq + d] = __float2bfloat16_rn(q);
+            Ks[i * L.ldq + d] = __float2bfloat16_rn(k);
+        }
+        for (int idx = tid; idx < LC_C * LC_VS; idx += LC_THREADS) {
+            const int i = idx / LC_VS, c = idx % LC_VS;
+            float v = 0.f;
+            if (i < n && c0 + c < vdim) v = ls_silu(__bfloat162float(proj[(size_t)(chunk0 + i) * ld + v_off + c]));
+            const __nv_bfloat16 vb = __float2bfloat16_rn(v);
+            Vs[i * L.ldv + c] = vb;
+            // the value's share of the new state: v_j * decay^(n - 1 - j)
+            lc_split(i < n ? __bfloat162float(vb) * pw[n - 1 - i] : 0.f, Vh[i * L.ldv + c], Vl[i * L.ldv + c]);
+        }
+        for (int idx = tid; idx < dim * LC_VS; idx += LC_THREADS) {
+            const int d = idx / LC_VS, c = idx % LC_VS;
+            lc_split(Sf[d * L.lds_f + c], Sh[d * L.lds_h + c], Sl[d * L.lds_h + c]);
+        }
+        __syncthreads();
+        // ---- A = Q K^T (the tiles on and below the diagonal) and Q S0
+        for (int tile = warp; tile < (LC_C / 16) * (LC_C / 16); tile += LC_THREADS / 32) {
+            const int ti = tile / (LC_C / 16), tj = tile % (LC_C / 16);
+            wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
+            wmma::fill_fragment(acc, 0.f);
+            if (tj <= ti) {
+                for (int kk = 0; kk < d_tiles; ++kk) {
+                    wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::row_major> a;
+                    wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::col_major> b;
+                    wmma::load_matrix_sync(a, Qs + ti * 16 * L.ldq + kk * 16, L.ldq);
+                    wmma::load_matrix_sync(b, Ks + tj * 16 * L.ldq + kk * 16, L.ldq);
+                    wmma::mma_sync(acc, a, b, acc);
+                }
+            }
+            wmma::store_matrix_sync(Af + ti * 16 * L.lda_f + tj * 16, acc, L.lda_f, wmma::mem_row_major);
+        }
+        for (int tile = warp; tile < (LC_C / 16) * (LC_VS / 16); tile += LC_THREADS / 32) {
+            const int ti = tile / (LC_VS / 16), tj = tile % (LC_VS / 16);
+            wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
+            wmma::fill_fragment(acc, 0.f);
+            for (int kk = 0; kk < d_tiles; ++kk) {
+                wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::row_major> a;
+                wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::row_major> b;
+                wmma::load_matrix_sync(a, Qs + ti * 16 * L.ldq + kk * 16, L.ldq);
+                wmma::load_matrix_sync(b, Sh + kk * 16 * L.lds_h + tj * 16, L.lds_h);
+                wmma::mma_sync(acc, a, b, acc);
+                wmma::load_matrix_sync(b, Sl + kk * 16 * L.lds_h + tj * 16, L.lds_h);
+                wmma::mma_sync(acc, a, b, acc);
+            }
+            wmma::store_matrix_sync(Of + ti * 16 * L.ldo + tj * 16, acc, L.ldo, wmma::mem_row_major);
+        }
+        __syncthreads();
+        // ---- decays, in float32: A'[i, j] = A[i, j] * decay^(i - j) for j <= i, in two halves; (Q S0)[i, :] *= decay^(i + 1)
+        for (int idx = tid; idx < LC_C * LC_C; idx += LC_THREADS) {
+            const int i = idx / LC_C, j = idx % LC_C;
+            lc_split(j <= i ? Af[i * L.lda_f + j] * pw[i - j] : 0.f, Ah[i * L.lda_h + j], Al[i * L.lda_h + j]);
+        }
+        for (int idx = tid; idx < LC_C * LC_VS; idx += LC_THREADS) {
+            const int i = idx / LC_VS, c = idx % LC_VS;
+            Of[i * L.ldo + c] *= pw[i + 1];
+        }
+        __syncthreads();
+        // ---- O += A' V;  S = decay^n S + K^T V'
+        for (int tile = warp; tile < (LC_C / 16) * (LC_VS / 16); tile += LC_THREADS / 32) {
+            const int ti = tile / (LC_VS / 16), tj = tile % (LC_VS / 16);
+            wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
+            wmma::load_matrix_sync(acc, Of + ti * 16 * L.ldo + tj * 16, L.ldo, wmma::mem_row_major);
+            for (int kk = 0; kk <= ti; ++kk) {                   // A' is zero above the diagonal
+                wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::row_major> a;
+                wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::row_major> b;
+                wmma::load_matrix_sync(b, Vs + kk * 16 * L.ldv + tj * 16, L.ldv);
+                wmma::load_matrix_sync(a, Ah + ti * 16 * L.lda_h + kk * 16, L.lda_h);
+                wmma::mma_sync(acc, a, b, acc);
+                wmma::load_matrix_sync(a, Al + ti * 16 * L.lda_h + kk * 16, L.lda_h);
+                wmma::mma_sync(acc, a, b, acc);
+            }
+            wmma::store_matrix_sync(Of + ti * 16 * L.ldo + tj * 16, acc, L.ldo, wmma::mem_row_major);
+        }
+        const float shrink = pw[n];
+        for (int tile = warp; tile < d_tiles * (LC_VS / 16); tile += LC_THREADS / 32) {
+            const int ti = tile / (LC_VS / 16), tj = tile % (LC_VS / 16);
+            wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
+            wmma::load_matrix_sync(acc, Sf + ti * 16 * L.lds_f + tj * 16, L.lds_f, wmma::mem_row_major);
+#pragma unroll
+            for (int e = 0; e < acc.num_elements; ++e) acc.x[e] *= shrink;
+            for (int kk = 0; kk < LC_C / 16; ++kk) {
+                wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::col_major> a;     // K^T: element (d, j) = K[j][d]
+                wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::row_major> b;
+                wmma::load_matrix_sync(a, Ks + kk * 16 * L.ldq + ti * 16, L.ldq);
+                wmma::load_matrix_sync(b, Vh + kk * 16 * L.ldv + tj * 16, L.ldv);
+                wmma::mma_sync(acc, a, b, acc);
+                wmma::load_matrix_sync(b, Vl + kk * 16 * L.ldv + tj * 16, L.ldv);
+                wmma::mma_sync(acc, a, b, acc);
+            }
+            wmma::store_matrix_sync(Sf + ti * 16 * L.lds_f + tj * 16, acc, L.lds_f, wmma::mem_row_major);
+        }
+        __syncthreads();
+        for (int idx = tid; idx < n * LC_VS; idx += LC_THREADS) {
+            const int i = idx / LC_VS, c = idx % LC_VS;
+            if (c0 + c < vdim) out[((size_t)(chunk0 + i) * heads + head) * vdim + c0 + c] = Of[i * L.ldo + c];
+        }
+    }
+    if (write_state) {
+        for (int idx = tid; idx < dim * LC_VS; idx += LC_THREADS) {
+            const int d = idx / LC_VS, c = idx % LC_VS;
+            if (c0 + c < vdim) S[(size_t)d * vdim + c0 + c] = Sf[d * L.lds_f + c];
+        }
+    }
+}
+
+// The chunked form: bfloat16 projections, dim a multiple of 16 up to 256. Same arguments as ttb_lightning_scan.
+TTB_EXPORT int ttb_lightning_chunks_supports(int dim, int vdim) {
+    return dim >= 16 && dim <= 256 && (dim & 15) == 0 && vdim >= 1 && lc_layout(dim).total <= 200 * 1024;
+}
+
+TTB_EXPORT int ttb_lightning_chunks(const void* proj, int ld, const int* cu_seqlens, const int* seg_slot, float* state,
+                                    const float* decay, float* out, int segments, int heads, int dim, int vdim, int write_state,
+                                    cudaStream_t stream) {
+    if (segments == 0) return TTB_OK;
+    if (!proj || !cu_seqlens || !seg_slot || !state || !decay || !out) return TTB_ERR_ARGUMENT;
+    if (!ttb_lightning_chunks_supports(dim, vdim) || heads < 1 || heads > 65535 || segments > 65535) return TTB_ERR_UNSUPPORTED;
+    const LcLayout L = lc_layout(dim);
+    static TtbOncePerDevice once;
+    if (once.pending()) {
+        cudaError_t e = cudaFuncSetAttribute(lightning_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return (int)e;
+        once.mark();
+    }
+    if (L.total > 200 * 1024) return TTB_ERR_UNSUPPORTED;
+    dim3 grid((vdim + LC_VS - 1) / LC_VS, heads, segments);
+    ttb_launch(lightning_chunk_kernel, grid, LC_THREADS, L.total, stream, (const __nv_bfloat16*)proj, ld, cu_seqlens, seg_slot, state,
+               decay, out, heads, dim, vdim, write_state);
+    return ttb_launch_status();
+}

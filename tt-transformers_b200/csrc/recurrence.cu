@@ -8,6 +8,10 @@
 //   a = exp(-rate[c] * sigmoid(gr + br));  S = a S + sqrt(1 - a^2) * sigmoid(gi + bi) * u;  out = S * gelu_tanh(y' + b_y)
 //   with the gates' float32 pre-activations [tokens, blocks, 2 s] (decay rows, then input rows, per block). At the end
 //   it stores S and the convolution's new tail (the last taps - 1 inputs of what the request has seen).
+//   Long segments are cut into parts of part_len tokens that run side by side (blockIdx.z): the recurrence is linear in
+//   S, so part p first (phase 1) walks its tokens from S = 0 and leaves (A_p, B_p) = (product of its a, its end state)
+//   in scratch memory; then (phase 2) every part folds the parts before it into its start state, S = A_q S + B_q from
+//   the request's kept state on, and walks its tokens again, this time writing out. Phase 0: one part, no scratch.
 // Gates, decays, the state and the recurrence are float32.
 #include "common.cuh"
 
@@ -48,12 +52,15 @@ gated_recurrence_kernel(const T* __restrict__ u, const float* __restrict__ gates
                         long long gate_ld_block, const float* __restrict__ gate_bias,
                         const float* __restrict__ rate, const T* __restrict__ yx, int ldyx, const float* __restrict__ bias_yx,
                         const int* __restrict__ cu_seqlens, const int* __restrict__ seg_slot, float* __restrict__ state,
-                        T* __restrict__ tail, T* __restrict__ out, int channels, int block_size, int taps, int write_state) {
+                        T* __restrict__ tail, T* __restrict__ out, int channels, int block_size, int taps, int write_state,
+                        float* __restrict__ scratch, int part_len, int phase) {
     pdl_wait();
     pdl_launch_dependents();
-    const int seg = blockIdx.y, c = blockIdx.x * RC_THREADS + threadIdx.x;
+    const int seg = blockIdx.y, c = blockIdx.x * RC_THREADS + threadIdx.x, part = blockIdx.z, parts = gridDim.z;
     if (c >= channels) return;
-    const int t_begin = cu_seqlens[seg], t_end = cu_seqlens[seg + 1];
+    const int seg_begin = cu_seqlens[seg], seg_end = cu_seqlens[seg + 1];
+    const int t_begin = phase == 0 ? seg_begin : seg_begin + part * part_len;
+    const int t_end = phase == 0 ? seg_end : min(seg_end, t_begin + part_len);
     if (t_begin >= t_end) return;
     const int slot = seg_slot[seg];
     const int b = c / block_size, i = c % block_size;
@@ -61,7 +68,16 @@ gated_recurrence_kernel(const T* __restrict__ u, const float* __restrict__ gates
     const float br = gate_bias[g_r], bi = gate_bias[g_i], k = rate[c], by = bias_yx[c];
     const float* gate_r = gates + (size_t)b * gate_ld_block + i;                   // the product may be strided by token and block
     const float* gate_i = gate_r + block_size;
-    float S = state[(size_t)slot * channels + c];
+    float S = 0.f, A = 1.f;
+    if (phase == 0) S = state[(size_t)slot * channels + c];
+    if (phase == 2) {
+        // the state as phase 1 found it (the part that ends the segment overwrites the slot while others still start)
+        S = scratch[(((size_t)seg * (parts + 1) + parts) * channels + c) * 2];
+        for (int q = 0; q < part; ++q) {
+            const float* ab = scratch + (((size_t)seg * (parts + 1) + q) * channels + c) * 2;
+            S = fmaf(ab[0], S, ab[1]);
+        }
+    }
 #pragma unroll 4
     for (int t = t_begin; t < t_end; ++t) {
         const float gr = gate_r[(size_t)t * gate_ld_token] + br, gi = gate_i[(size_t)t * gate_ld_token] + bi;
@@ -70,14 +86,26 @@ gated_recurrence_kernel(const T* __restrict__ u, const float* __restrict__ gates
         const float a = expf(log_a);
         const float mult = sqrtf(fmaxf(1.f - a * a, 0.f));
         S = fmaf(a, S, mult * (in * to_float(u[(size_t)t * channels + c])));
+        if (phase == 1) {
+            A *= a;
+            continue;
+        }
         const float y = rc_gelu_tanh(to_float(yx[(size_t)t * ldyx + c]) + by);
         out[(size_t)t * channels + c] = from_float<T>(S * y);
     }
-    if (!write_state) return;
+    if (phase == 1) {
+        float* ab = scratch + (((size_t)seg * (parts + 1) + part) * channels + c) * 2;
+        ab[0] = A;
+        ab[1] = S;
+        if (part == 0) scratch[(((size_t)seg * (parts + 1) + parts) * channels + c) * 2] = state[(size_t)slot * channels + c];
+        return;
+    }
+    if (!write_state || t_end != seg_end) return;            // the part that holds the segment's last token keeps the state
     state[(size_t)slot * channels + c] = S;
     if (taps > 1) {
         // the kept inputs followed by this step's: the last taps - 1 of them stay
-        const int keep = taps - 1, len = t_end - t_begin;
+        const int keep = taps - 1, len = seg_end - seg_begin;
+        const int t_begin = seg_begin;
         const float bx = bias_yx[channels + c];
         T* kept = tail + (size_t)slot * keep * channels;
         T fresh[RC_MAX_TAPS];
@@ -115,19 +143,24 @@ TTB_EXPORT int ttb_gated_recurrence(const void* u, int dtype, const float* gates
                                     const float* gate_bias, const float* rate,
                                     const void* yx, int ldyx, const float* bias_yx, const int* cu_seqlens, const int* seg_slot,
                                     float* state, void* tail, void* out, int segments, int channels, int blocks, int taps,
-                                    int write_state, cudaStream_t stream) {
+                                    int write_state, float* scratch, int parts, int part_len, cudaStream_t stream) {
     if (segments == 0) return TTB_OK;
     if (!u || !gates || !gate_bias || !rate || !yx || !bias_yx || !cu_seqlens || !seg_slot || !state || !tail || !out)
         return TTB_ERR_ARGUMENT;
     if (taps < 1 || taps > RC_MAX_TAPS || blocks < 1 || channels % blocks || segments > 65535) return TTB_ERR_UNSUPPORTED;
-    dim3 grid((channels + RC_THREADS - 1) / RC_THREADS, segments);
-    if (dtype == TTB_DTYPE_BF16)
-        ttb_launch(gated_recurrence_kernel<__nv_bfloat16>, grid, RC_THREADS, 0, stream, (const __nv_bfloat16*)u, gates, gate_ld_token, gate_ld_block, gate_bias, rate,
-                   (const __nv_bfloat16*)yx, ldyx, bias_yx, cu_seqlens, seg_slot, state, (__nv_bfloat16*)tail, (__nv_bfloat16*)out,
-                   channels, channels / blocks, taps, write_state);
-    else if (dtype == TTB_DTYPE_F32)
-        ttb_launch(gated_recurrence_kernel<float>, grid, RC_THREADS, 0, stream, (const float*)u, gates, gate_ld_token, gate_ld_block, gate_bias, rate, (const float*)yx,
-                   ldyx, bias_yx, cu_seqlens, seg_slot, state, (float*)tail, (float*)out, channels, channels / blocks, taps, write_state);
-    else return TTB_ERR_UNSUPPORTED;
+    if (parts < 1 || parts > 65535 || (parts > 1 && (!scratch || part_len < 1))) return TTB_ERR_ARGUMENT;
+    dim3 grid((channels + RC_THREADS - 1) / RC_THREADS, segments, parts);
+    // parts > 1: scratch holds segments * (parts + 1) * channels * 2 floats; two launches
+    for (int phase = parts > 1 ? 1 : 0; phase <= (parts > 1 ? 2 : 0); ++phase) {
+        if (dtype == TTB_DTYPE_BF16)
+            ttb_launch(gated_recurrence_kernel<__nv_bfloat16>, grid, RC_THREADS, 0, stream, (const __nv_bfloat16*)u, gates, gate_ld_token,
+                       gate_ld_block, gate_bias, rate, (const __nv_bfloat16*)yx, ldyx, bias_yx, cu_seqlens, seg_slot, state,
+                       (__nv_bfloat16*)tail, (__nv_bfloat16*)out, channels, channels / blocks, taps, write_state, scratch, part_len, phase);
+        else if (dtype == TTB_DTYPE_F32)
+            ttb_launch(gated_recurrence_kernel<float>, grid, RC_THREADS, 0, stream, (const float*)u, gates, gate_ld_token, gate_ld_block,
+                       gate_bias, rate, (const float*)yx, ldyx, bias_yx, cu_seqlens, seg_slot, state, (float*)tail, (float*)out,
+                       channels, channels / blocks, taps, write_state, scratch, part_len, phase);
+        else return TTB_ERR_UNSUPPORTED;
+    }
     return ttb_launch_status();
 }

@@ -6,6 +6,7 @@
 //   the `top` largest s among the rest are chosen (the lower index among equals)
 //   weight_j = s_j / (sum of the chosen s + floor)
 //
+// Rows whose scores are not numbers (padded rows of a captured step) get scores of zero and choose the first experts.
 // RG_TOKENS tokens a block share one pass over W_r; a warp per logit row, then a warp per token selects. Every logit is
 // summed in the same order whatever else the batch holds.
 #include "common.cuh"
@@ -60,7 +61,10 @@ route_grouped_kernel(const T* __restrict__ x, int ldx, const float* __restrict__
         float total = 0.f;
         for (int e = lane; e < experts; e += 32) total += expf(zt[e] - top_z);
         total = warp_sum(total);
-        for (int e = lane; e < experts; e += 32) zt[e] = expf(zt[e] - top_z) / total;
+        for (int e = lane; e < experts; e += 32) {
+            const float sv = expf(zt[e] - top_z) / total;
+            zt[e] = sv == sv ? sv : 0.f;          // a row that is not a number (a padded row on nobody's state) still chooses valid experts
+        }
         __syncwarp();
         // the groups' scores; the best `keep` of them stay open
         for (int g = lane; g < groups; g += 32) {
@@ -106,6 +110,7 @@ route_grouped_kernel(const T* __restrict__ x, int ldx, const float* __restrict__
                 const int oe = __shfl_xor_sync(0xffffffffu, best, o);
                 if (oe != 0x7fffffff && (best == 0x7fffffff || os > best_s || (os == best_s && oe < best))) { best = oe; best_s = os; }
             }
+            if (best == 0x7fffffff) best = 0;                   // cannot happen: keep * per_group >= top; never index with it
             if (lane == 0) {
                 op[best] = 0;
                 choice[(size_t)t * top + j] = best;

@@ -99,7 +99,8 @@ class CudaKernels:
                      "ttb_latent_attention_mma", "ttb_latent_attention_mma_supports", "ttb_moe_gemv", "ttb_moe_gemm_tcgen05", "ttb_latent_out",
                      "ttb_latent_attention_mma_tokens_per_tile", "ttb_stream_add_norm", "ttb_gated_rmsnorm",
                      "ttb_mean_rmsnorm_pair", "ttb_activation", "ttb_lightning_scan", "ttb_causal_conv", "ttb_gated_recurrence",
-                     "ttb_paged_attention_generic_ext", "ttb_qk_norm_rope_write", "ttb_route_grouped", "ttb_moe_gemv_plain"):
+                     "ttb_paged_attention_generic_ext", "ttb_qk_norm_rope_write", "ttb_route_grouped", "ttb_moe_gemv_plain",
+                     "ttb_paged_attention_mma_ext", "ttb_lightning_chunks", "ttb_lightning_chunks_supports"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -110,6 +111,8 @@ class CudaKernels:
         self.launches = 0     # how many of our kernels were launched (counted for reports)
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.use_mma_attention = True
+        # linear attention over prompt portions chunk by chunk on the tensor cores (False: token by token everywhere)
+        self.use_lightning_chunks = os.environ.get("TTB200_LIGHTNING_CHUNKS", "1") == "1"
         # latent attention in bfloat16 on the tensor cores (False: the float32-arithmetic kernel everywhere)
         self.use_mma_latent_attention = os.environ.get("TTB200_MMA_LATENT", "1") == "1"
         # prompt portions at head size 64: the TMA + tcgen05 attention kernel (False: the mma.sync one)
@@ -932,6 +935,9 @@ class CudaKernels:
         return out
 
     # ------------------------------------------------------------------ recurrent mixers
+    RECURRENCE_PART = 64            # tokens of one part of a long segment in the gated recurrence
+    LIGHTNING_SCAN_TOKENS = 16      # steps whose longest segment is at most this long walk token by token
+
     def lightning_attention(self, proj, batch, view, heads, dim, vdim, decays, write_state=True):
         """proj [T, q | k | v | ...] before their silu; the state float32 [slots, heads, dim, vdim] of view continues
         per segment: S = decay S + k v^T, o = S^T q. -> float32 [T, heads * vdim]."""
@@ -941,6 +947,14 @@ class CudaKernels:
         if view.state.dtype != torch.float32 or tuple(view.state.shape[1:]) != (heads, dim, vdim) or not view.state.is_contiguous():
             raise KernelError("lightning_attention: the state must be float32 [slots, heads, dim, vdim]")
         out = torch.empty(tokens, heads * vdim, dtype=torch.float32, device=self.device)
+        if (self.use_lightning_chunks and proj.dtype == torch.bfloat16 and batch.max_seg_len > self.LIGHTNING_SCAN_TOKENS
+                and self.lib.ttb_lightning_chunks_supports(dim, vdim)):
+            # prompt portions: chunk by chunk on the tensor cores (decoded tokens and float32 walk token by token)
+            self._check(self.lib.ttb_lightning_chunks(
+                self._p(proj), proj.stride(0), self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state),
+                self._p(decays), self._p(out), batch.num_segments, heads, dim, vdim, 1 if write_state else 0,
+                self._stream()), "lightning_chunks")
+            return out
         self._check(self.lib.ttb_lightning_scan(
             self._p(proj), _dtype_code(proj.dtype), proj.stride(0), self._p(batch.cu_seqlens), self._p(view.slots),
             self._p(view.state), self._p(decays), self._p(out), batch.num_segments, heads, dim, vdim, 1 if write_state else 0,
@@ -970,12 +984,18 @@ class CudaKernels:
         if gates.dtype != torch.float32 or gates.stride(2) != 1 or not u.is_contiguous() or yx.stride(1) != 1:
             raise KernelError("gated_recurrence: float32 gates contiguous along their last axis, contiguous u")
         out = torch.empty(tokens, channels, dtype=u.dtype, device=self.device)
+        # long segments run as parts of RECURRENCE_PART tokens side by side (two launches: the parts' own products
+        # and end states, then the walk that writes out from each part's folded start state)
+        parts = -(-batch.max_seg_len // self.RECURRENCE_PART) if batch.max_seg_len >= 2 * self.RECURRENCE_PART else 1
+        scratch = torch.empty(batch.num_segments * (parts + 1) * channels * 2, dtype=torch.float32, device=self.device) if parts > 1 else None
+        if parts > 1:
+            self.launches += 1
         self._check(self.lib.ttb_gated_recurrence(
             self._p(u), _dtype_code(u.dtype), self._p(gates), ctypes.c_longlong(gates.stride(0)),
             ctypes.c_longlong(gates.stride(1)), self._p(gate_bias), self._p(rate), self._p(yx), yx.stride(0),
             self._p(bias_yx), self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state), self._p(view.tail),
-            self._p(out), batch.num_segments, channels, blocks, view.taps, 1 if write_state else 0, self._stream()),
-            "gated_recurrence")
+            self._p(out), batch.num_segments, channels, blocks, view.taps, 1 if write_state else 0, self._p(scratch), parts,
+            self.RECURRENCE_PART, self._stream()), "gated_recurrence")
         return out
 
     # ------------------------------------------------------------------ attention with a sink, a cap, chunks
@@ -1006,6 +1026,28 @@ class CudaKernels:
         if view.keys.dtype != qkv.dtype:
             raise KernelError("sink_attention: cache pages and queries differ in dtype")
         out = torch.empty(tokens, heads * vdim, dtype=qkv.dtype, device=self.device)
+        if (self.use_mma_attention and qkv.dtype == torch.bfloat16 and dim == vdim and qkv.stride(0) % 8 == 0
+                and view.keys.is_contiguous() and view.values.is_contiguous()
+                and self.lib.ttb_attention_mma_supports(heads, kv_heads, dim)):
+            # keys and values of one size that the tensor-core kernel takes: 64-row tiles for prompt portions, the
+            # decode shape for single tokens; key splits sized by what a query can see at most
+            decode_shape, seg, tok0, n_tiles, splits = self._attention_plan(batch, heads // kv_heads, kv_heads, dim)
+            reach = min(x for x in (batch.max_context, view.chunk, view.window) if x)
+            splits = max(1, min(splits, reach // 256))
+            partial_o = partial_ml = None
+            if splits > 1:
+                partial_o = torch.empty(tokens * heads * splits * dim, dtype=torch.float32, device=self.device)
+                partial_ml = torch.empty(tokens * heads * splits * 2, dtype=torch.float32, device=self.device)
+            self._check(self.lib.ttb_paged_attention_mma_ext(
+                self._p(qkv), qkv.stride(0), self._p(out), self._p(batch.cu_seqlens), self._p(batch.seg_pos0),
+                self._p(view.keys), self._p(view.values), self._p(view.block_table), view.block_table.shape[1],
+                view.page_size, self._p(seg), self._p(tok0), n_tiles, tokens, heads, kv_heads, dim, ctypes.c_float(scale),
+                int(view.window or 0), 1 if decode_shape else 0, splits, self._p(partial_o), self._p(partial_ml),
+                view.keys.shape[0], self._p(self.status), ctypes.c_float(softcap or 0.0), int(view.chunk or 0),
+                self._p(sinks), self._stream()), "sink_attention_mma")
+            if splits > 1:
+                self.launches += 1
+            return out
         self._check(self.lib.ttb_paged_attention_generic_ext(
             self._p(qkv), qkv.stride(0), self._p(out), _dtype_code(qkv.dtype), self._p(batch.positions),
             self._p(batch.seg_of_token), self._p(view.keys), self._p(view.values), self._p(view.block_table),

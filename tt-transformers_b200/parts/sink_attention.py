@@ -67,6 +67,14 @@ class SinkAttention(Mixer):
     def cache_request(self):
         return PagedKV(self.kv_heads, self.dim, self.window, value_dim=self.vdim, chunk=self.chunk)
 
+    def step_tables_signature(self):
+        return ("attention", self.heads // self.kv_heads)
+
+    def step_tables(self, seg_lens, seg_pos0, fixed_tokens=0):
+        """The query-tile lists that the tensor-core attention kernels want for this step (they travel with the
+        step's metadata in its one copy to the device)."""
+        return self.runtime.kernels.attention_tables(seg_lens, seg_pos0, self.heads // self.kv_heads, fixed_tokens)
+
     def forward(self, x, batch, cache, write_cache=True):
         k = self.runtime.kernels
         rotation = self.position.rotation() if self.position is not None else None
