@@ -399,18 +399,19 @@ TTB_EXPORT int ttb_gemm_tcgen05(const void* A, const void* W, void* C, int out_d
 // W_e (rows e * rows_per_expert .. of one stacked matrix). The grouping kernel leaves a table of row tiles
 // (expert, first row) and their count on the device, so no size is read back by the host; the grid is sized for the
 // most tiles there can be. A tile's box of 128 rows may reach into the next expert's rows: those rows are computed
-// and not stored. FIRST: W_e = [gate rows; up rows], the epilogue writes g' sigmoid(alpha g') (u' + 1) with
-// g' = min(g, L), u' = clamp(u, -L, L) into the hidden rows (grouped order). Otherwise: float32 results go to the
-// row that `sorted` names for each grouped row (the pair's own row).
-template <bool FIRST>
+// and not stored. MODE 1: W_e = [gate rows; up rows], the epilogue writes g' sigmoid(alpha g') (u' + 1) with
+// g' = min(g, L), u' = clamp(u, -L, L) into the hidden rows (grouped order). MODE 2: W_e = [rows] without a gate, the
+// epilogue writes relu(z)^2 into the hidden rows. MODE 0: float32 results go to the row that `sorted` names for each
+// grouped row (the pair's own row).
+template <int MODE>
 __global__ void __launch_bounds__(TC_THREADS)
 moe_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                         void* __restrict__ out_raw, const int* __restrict__ offsets, const int* __restrict__ sorted,
                         const int* __restrict__ tile_info, const int* __restrict__ num_m_tiles, int N, int K, int ldc,
                         int rows_per_expert, int n_tiles, float limit, float alpha, int* __restrict__ error_flag) {
     using Cfg = TcCfg;
-    using TO = typename std::conditional<FIRST, __nv_bfloat16, float>::type;
-    constexpr int OUT_COLS = FIRST ? Cfg::ACC_COLS / 2 : Cfg::ACC_COLS;
+    using TO = typename std::conditional<MODE != 0, __nv_bfloat16, float>::type;
+    constexpr int OUT_COLS = MODE == 1 ? Cfg::ACC_COLS / 2 : Cfg::ACC_COLS;
     TO* out = reinterpret_cast<TO*>(out_raw);
     extern __shared__ unsigned char tc_raw[];
     unsigned char* tiles = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~(uintptr_t)1023);
@@ -467,7 +468,7 @@ moe_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
                     mbar_expect_tx(bar, Cfg::STAGE_BYTES);
                     unsigned char* stage = tiles + s * Cfg::STAGE_BYTES;
                     tma_load_2d(tc_smem(stage), &map_a, kb * TC_BK, row0, bar);
-                    if (FIRST) {
+                    if (MODE == 1) {
                         tma_load_2d(tc_smem(stage + Cfg::A_BYTES), &map_w, kb * TC_BK, w_row, bar);
                         tma_load_2d(tc_smem(stage + Cfg::A_BYTES + Cfg::B_BYTES / 2), &map_w, kb * TC_BK, w_row + N, bar);
                     } else {
@@ -528,7 +529,7 @@ moe_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
             }
             tc_fence_after();
             // where this lane's row goes: the hidden rows keep the grouped order, results go to the pair's own row
-            const long long my_dst = row0 + lane < row_end ? (FIRST ? (long long)(row0 + lane) : (long long)sorted[row0 + lane]) : -1;
+            const long long my_dst = row0 + lane < row_end ? (MODE != 0 ? (long long)(row0 + lane) : (long long)sorted[row0 + lane]) : -1;
             const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_COLS;
 #pragma unroll 1
             for (int c0 = 0; c0 < OUT_COLS; c0 += LINE_COLS) {
@@ -537,7 +538,7 @@ moe_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
                     uint32_t accv[32];
                     tc_load32(lane_addr + c0 + h * 32, accv);
                     float v[32];
-                    if (FIRST) {
+                    if (MODE == 1) {
                         uint32_t up[32];
                         tc_load32(lane_addr + OUT_COLS + c0 + h * 32, up);
 #pragma unroll
@@ -545,6 +546,12 @@ moe_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
                             const float g = fminf(__uint_as_float(accv[j]), limit);
                             const float u = fminf(fmaxf(__uint_as_float(up[j]), -limit), limit);
                             v[j] = __fdividef(g, 1.f + __expf(-alpha * g)) * (u + 1.f);
+                        }
+                    } else if (MODE == 2) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float z = fmaxf(__uint_as_float(accv[j]), 0.f);
+                            v[j] = z * z;
                         }
                     } else {
 #pragma unroll
@@ -590,7 +597,8 @@ moe_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
 }
 
 // A [rows, K] in grouped order; W [experts * rows_per_expert, K] (first: rows_per_expert = 2 N, gate then up rows;
-// otherwise N); C: first ? bfloat16 hidden [rows, N] : float32 [rows, N] written by `sorted`. tile_info / num_m_tiles:
+// first 2: rows_per_expert = N and relu(z)^2 in the epilogue; otherwise N); C: first ? bfloat16 hidden [rows, N] :
+// float32 [rows, N] written by `sorted`. tile_info / num_m_tiles:
 // what the grouping kernel left for row tiles of 128. max_m_tiles: the most row tiles there can be.
 TTB_EXPORT int ttb_moe_gemm_tcgen05(const void* A, int lda, const void* W, int ldw, void* C, int ldc, int first,
                                     const int* offsets, const int* sorted, const int* tile_info, const int* num_m_tiles,
@@ -599,27 +607,32 @@ TTB_EXPORT int ttb_moe_gemm_tcgen05(const void* A, int lda, const void* W, int l
     if (rows == 0 || N == 0) return TTB_OK;
     if (!A || !W || !C || !offsets || !sorted || !tile_info || !num_m_tiles || !error_flag) return TTB_ERR_ARGUMENT;
     if (K < 8 || (K & 7) || (lda & 7) || (ldw & 7) || !aligned16(A) || !aligned16(W)) return TTB_ERR_UNSUPPORTED;
-    const int rows_per_expert = first ? 2 * N : N;
+    if (first < 0 || first > 2) return TTB_ERR_ARGUMENT;
+    const int rows_per_expert = first == 1 ? 2 * N : N;
     if ((long long)experts * rows_per_expert > 2147483647LL) return TTB_ERR_UNSUPPORTED;
     CUtensorMap map_a, map_w;
     if (!tc_make_map(&map_a, A, rows, K, lda, TC_BM)) return TTB_ERR_UNSUPPORTED;
-    if (!tc_make_map(&map_w, W, experts * rows_per_expert, K, ldw, first ? TcCfg::ACC_COLS / 2 : TcCfg::ACC_COLS)) return TTB_ERR_UNSUPPORTED;
-    const int out_cols = first ? TcCfg::ACC_COLS / 2 : TcCfg::ACC_COLS;
+    if (!tc_make_map(&map_w, W, experts * rows_per_expert, K, ldw, first == 1 ? TcCfg::ACC_COLS / 2 : TcCfg::ACC_COLS)) return TTB_ERR_UNSUPPORTED;
+    const int out_cols = first == 1 ? TcCfg::ACC_COLS / 2 : TcCfg::ACC_COLS;
     const int n_tiles = (N + out_cols - 1) / out_cols;
     const long long most = (long long)max_m_tiles * n_tiles;
     const int blocks = most < tc_sm_count() ? (int)most : tc_sm_count();
     static TtbOncePerDevice configured;
     if (configured.pending()) {
-        cudaError_t e = cudaFuncSetAttribute(moe_gemm_tcgen05_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg::SMEM_BYTES);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(moe_gemm_tcgen05_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg::SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(moe_gemm_tcgen05_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg::SMEM_BYTES);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(moe_gemm_tcgen05_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg::SMEM_BYTES);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(moe_gemm_tcgen05_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg::SMEM_BYTES);
         if (e != cudaSuccess) return (int)e;
         configured.mark();
     }
-    if (first)
-        ttb_launch(moe_gemm_tcgen05_kernel<true>, dim3(blocks), dim3(TC_THREADS), (size_t)TcCfg::SMEM_BYTES, stream, map_a, map_w,
+    if (first == 2)
+        ttb_launch(moe_gemm_tcgen05_kernel<2>, dim3(blocks), dim3(TC_THREADS), (size_t)TcCfg::SMEM_BYTES, stream, map_a, map_w,
+                   C, offsets, sorted, tile_info, num_m_tiles, N, K, ldc, rows_per_expert, n_tiles, limit, alpha, error_flag);
+    else if (first)
+        ttb_launch(moe_gemm_tcgen05_kernel<1>, dim3(blocks), dim3(TC_THREADS), (size_t)TcCfg::SMEM_BYTES, stream, map_a, map_w,
                    C, offsets, sorted, tile_info, num_m_tiles, N, K, ldc, rows_per_expert, n_tiles, limit, alpha, error_flag);
     else
-        ttb_launch(moe_gemm_tcgen05_kernel<false>, dim3(blocks), dim3(TC_THREADS), (size_t)TcCfg::SMEM_BYTES, stream, map_a, map_w,
+        ttb_launch(moe_gemm_tcgen05_kernel<0>, dim3(blocks), dim3(TC_THREADS), (size_t)TcCfg::SMEM_BYTES, stream, map_a, map_w,
                    C, offsets, sorted, tile_info, num_m_tiles, N, K, ldc, rows_per_expert, n_tiles, limit, alpha, error_flag);
     return ttb_launch_status();
 }

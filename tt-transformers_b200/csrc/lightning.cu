@@ -114,6 +114,10 @@ TTB_EXPORT int ttb_lightning_scan(const void* proj, int dtype, int ld, const int
 // (v = hi + lo with hi = bf16(v), lo = bf16(v - hi): sixteen bits of mantissa, 2^-17 relative), each half with a
 // product of its own: A' = A * L^(i-j), V' = V * L^(C-1-j) and S0. The state itself stays float32 in shared memory
 // for the whole segment. A block owns LC_VS columns of one head's state of one segment and walks its chunks in order.
+// Long segments are cut into parts of part_len tokens (a multiple of the chunk) that run side by side (blockIdx.x):
+// the recurrence is linear in S, so in phase 1 every part walks its chunks from S = 0, keys and values only, and leaves
+// its end state in scratch memory; in phase 2 part p starts from S = decay^(p part_len) S_kept + sum_(q<p)
+// decay^((p-1-q) part_len) S_q and walks its chunks again, now with the queries. Phase 0: one part, no scratch.
 #include <mma.h>
 using namespace nvcuda;
 
@@ -156,7 +160,8 @@ __device__ __forceinline__ void lc_split(float v, __nv_bfloat16& hi, __nv_bfloat
 __global__ void __launch_bounds__(LC_THREADS)
 lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int* __restrict__ cu_seqlens,
                        const int* __restrict__ seg_slot, float* __restrict__ state, const float* __restrict__ decay,
-                       float* __restrict__ out, int heads, int dim, int vdim, int write_state) {
+                       float* __restrict__ out, int heads, int dim, int vdim, int write_state, float* __restrict__ scratch,
+                       int part_len, int parts, int phase) {
     extern __shared__ __align__(128) unsigned char lc_smem[];
     const LcLayout L = lc_layout(dim);
     __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(lc_smem + L.q);
@@ -176,15 +181,32 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
     pdl_wait();
     pdl_launch_dependents();
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int seg = blockIdx.z, head = blockIdx.y, c0 = blockIdx.x * LC_VS;
-    const int t_begin = cu_seqlens[seg], t_end = cu_seqlens[seg + 1];
+    const int seg = blockIdx.z, head = blockIdx.y, part = blockIdx.x % parts, c0 = (blockIdx.x / parts) * LC_VS;
+    const int seg_begin = cu_seqlens[seg], seg_end = cu_seqlens[seg + 1];
+    const int t_begin = seg_begin + part * part_len;
+    const int t_end = phase == 0 ? seg_end : min(seg_end, t_begin + part_len);
     if (t_begin >= t_end) return;
     float* S = state + (((size_t)seg_slot[seg] * heads + head) * dim) * vdim;
+    // scratch: [segment, head, part 0 .. parts (the last one: the state the request came with), dim, vdim]
+    float* parts_S = scratch + ((size_t)seg * heads + head) * (parts + 1) * dim * vdim;
     const float lambda = decay[head];
     for (int x = tid; x <= LC_C; x += LC_THREADS) pw[x] = x == 0 ? 1.f : powf(lambda, (float)x);
+    const float per_part = phase == 2 ? powf(lambda, (float)part_len) : 1.f;
     for (int idx = tid; idx < dim * LC_VS; idx += LC_THREADS) {
         const int d = idx / LC_VS, c = idx % LC_VS;
-        Sf[d * L.lds_f + c] = c0 + c < vdim ? S[(size_t)d * vdim + c0 + c] : 0.f;
+        float v = 0.f;
+        if (c0 + c < vdim) {
+            const size_t at = (size_t)d * vdim + c0 + c;
+            if (phase == 0) {
+                v = S[at];
+            } else if (phase == 1) {
+                if (part == 0) parts_S[(size_t)parts * dim * vdim + at] = S[at];      // kept for phase 2: the last part overwrites S
+            } else {
+                v = parts_S[(size_t)parts * dim * vdim + at];
+                for (int q = 0; q < part; ++q) v = fmaf(per_part, v, parts_S[(size_t)q * dim * vdim + at]);
+            }
+        }
+        Sf[d * L.lds_f + c] = v;
     }
     const int q_off = head * dim, k_off = heads * dim + head * dim, v_off = 2 * heads * dim + head * vdim + c0;
     const int d_tiles = dim / 16;
@@ -218,6 +240,7 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
             lc_split(Sf[d * L.lds_f + c], Sh[d * L.lds_h + c], Sl[d * L.lds_h + c]);
         }
         __syncthreads();
+        if (phase != 1) {
         // ---- A = Q K^T (the tiles on and below the diagonal) and Q S0
         for (int tile = warp; tile < (LC_C / 16) * (LC_C / 16); tile += LC_THREADS / 32) {
             const int ti = tile / (LC_C / 16), tj = tile % (LC_C / 16);
@@ -260,8 +283,9 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
             Of[i * L.ldo + c] *= pw[i + 1];
         }
         __syncthreads();
+        }
         // ---- O += A' V;  S = decay^n S + K^T V'
-        for (int tile = warp; tile < (LC_C / 16) * (LC_VS / 16); tile += LC_THREADS / 32) {
+        for (int tile = warp; phase != 1 && tile < (LC_C / 16) * (LC_VS / 16); tile += LC_THREADS / 32) {
             const int ti = tile / (LC_VS / 16), tj = tile % (LC_VS / 16);
             wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
             wmma::load_matrix_sync(acc, Of + ti * 16 * L.ldo + tj * 16, L.ldo, wmma::mem_row_major);
@@ -295,12 +319,19 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
             wmma::store_matrix_sync(Sf + ti * 16 * L.lds_f + tj * 16, acc, L.lds_f, wmma::mem_row_major);
         }
         __syncthreads();
-        for (int idx = tid; idx < n * LC_VS; idx += LC_THREADS) {
+        for (int idx = tid; phase != 1 && idx < n * LC_VS; idx += LC_THREADS) {
             const int i = idx / LC_VS, c = idx % LC_VS;
             if (c0 + c < vdim) out[((size_t)(chunk0 + i) * heads + head) * vdim + c0 + c] = Of[i * L.ldo + c];
         }
     }
-    if (write_state) {
+    if (phase == 1) {
+        for (int idx = tid; idx < dim * LC_VS; idx += LC_THREADS) {
+            const int d = idx / LC_VS, c = idx % LC_VS;
+            if (c0 + c < vdim) parts_S[(size_t)part * dim * vdim + (size_t)d * vdim + c0 + c] = Sf[d * L.lds_f + c];
+        }
+        return;
+    }
+    if (write_state && t_end == seg_end) {
         for (int idx = tid; idx < dim * LC_VS; idx += LC_THREADS) {
             const int d = idx / LC_VS, c = idx % LC_VS;
             if (c0 + c < vdim) S[(size_t)d * vdim + c0 + c] = Sf[d * L.lds_f + c];
@@ -313,9 +344,10 @@ TTB_EXPORT int ttb_lightning_chunks_supports(int dim, int vdim) {
     return dim >= 16 && dim <= 256 && (dim & 15) == 0 && vdim >= 1 && lc_layout(dim).total <= 200 * 1024;
 }
 
+// parts > 1: scratch holds segments * heads * (parts + 1) * dim * vdim floats, part_len is a multiple of the chunk (64).
 TTB_EXPORT int ttb_lightning_chunks(const void* proj, int ld, const int* cu_seqlens, const int* seg_slot, float* state,
                                     const float* decay, float* out, int segments, int heads, int dim, int vdim, int write_state,
-                                    cudaStream_t stream) {
+                                    float* scratch, int parts, int part_len, cudaStream_t stream) {
     if (segments == 0) return TTB_OK;
     if (!proj || !cu_seqlens || !seg_slot || !state || !decay || !out) return TTB_ERR_ARGUMENT;
     if (!ttb_lightning_chunks_supports(dim, vdim) || heads < 1 || heads > 65535 || segments > 65535) return TTB_ERR_UNSUPPORTED;
@@ -327,8 +359,10 @@ TTB_EXPORT int ttb_lightning_chunks(const void* proj, int ld, const int* cu_seql
         once.mark();
     }
     if (L.total > 200 * 1024) return TTB_ERR_UNSUPPORTED;
-    dim3 grid((vdim + LC_VS - 1) / LC_VS, heads, segments);
-    ttb_launch(lightning_chunk_kernel, grid, LC_THREADS, L.total, stream, (const __nv_bfloat16*)proj, ld, cu_seqlens, seg_slot, state,
-               decay, out, heads, dim, vdim, write_state);
+    if (parts < 1 || (parts > 1 && (!scratch || part_len < LC_C || part_len % LC_C))) return TTB_ERR_ARGUMENT;
+    dim3 grid(((vdim + LC_VS - 1) / LC_VS) * parts, heads, segments);
+    for (int phase = parts > 1 ? 1 : 0; phase <= (parts > 1 ? 2 : 0); ++phase)
+        ttb_launch(lightning_chunk_kernel, grid, LC_THREADS, L.total, stream, (const __nv_bfloat16*)proj, ld, cu_seqlens, seg_slot,
+                   state, decay, out, heads, dim, vdim, write_state, scratch, part_len, parts, phase);
     return ttb_launch_status();
 }

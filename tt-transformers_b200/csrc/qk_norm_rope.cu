@@ -1,7 +1,8 @@
 // Per-head RMS norm of queries and keys, rotation by position, and the write of keys and values into cache pages,
 // for attention whose keys and values may differ in size.
 //
-// qkv [tokens, heads * dim | kv_heads * dim | kv_heads * vdim] of the compute type. One block per (token, head unit):
+// qkv [tokens, heads * dim | kv_heads * dim | kv_heads * vdim] of the compute type. One warp per (token, head unit),
+// four of them a block:
 //   query head:  q = rms(q) * w_q (optional), rotated, written back in place
 //   key head:    k = rms(k) * w_k (optional), rotated, written back in place and into its page row
 //   value head:  copied into its page row
@@ -19,11 +20,13 @@ qk_norm_rope_write_kernel(T* __restrict__ qkv, int ld, const int* __restrict__ p
                           const float* __restrict__ inv_freq, int rotary_dim, int heads, int kv_heads, int dim, int vdim,
                           T* __restrict__ key_pages, T* __restrict__ value_pages, const int* __restrict__ block_table,
                           int table_width, int page_size, int num_pages, int write_kv, int* __restrict__ status) {
-    extern __shared__ float qn_row[];          // [dim]
-    __shared__ float scratch[32];
+    extern __shared__ float qn_rows[];         // [warps][dim]
     pdl_wait();
     pdl_launch_dependents();
-    const int t = blockIdx.x, unit = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int t = blockIdx.x, unit = blockIdx.y * (QN_THREADS / 32) + warp;
+    if (unit >= heads + 2 * kv_heads) return;
+    float* qn_row = qn_rows + warp * dim;
     const int pos = positions[t];
     const bool is_q = unit < heads, is_k = !is_q && unit < heads + kv_heads;
     const int g = is_q ? unit : (is_k ? unit - heads : unit - heads - kv_heads);
@@ -35,11 +38,11 @@ qk_norm_rope_write_kernel(T* __restrict__ qkv, int ld, const int* __restrict__ p
             const int page_index = pos / page_size;
             int page = -1;
             if (page_index >= table_width) {
-                if (threadIdx.x == 0) atomicExch(status, 0x1000000 + t);
+                if (lane == 0) atomicExch(status, 0x1000000 + t);
             } else {
                 page = block_table[(size_t)seg_of_token[t] * table_width + page_index];
                 if ((unsigned)page >= (unsigned)num_pages) {
-                    if (threadIdx.x == 0) atomicExch(status, 0x2000000 + t);
+                    if (lane == 0) atomicExch(status, 0x2000000 + t);
                     page = -1;
                 }
             }
@@ -52,25 +55,25 @@ qk_norm_rope_write_kernel(T* __restrict__ qkv, int ld, const int* __restrict__ p
     if (!is_q && !is_k) {                       // a value head: a copy
         const T* src = qkv + (size_t)t * ld + (size_t)(heads + kv_heads) * dim + (size_t)g * vdim;
         if (dst_page != nullptr)
-            for (int d = threadIdx.x; d < vdim; d += QN_THREADS) dst_page[d] = src[d];
+            for (int d = lane; d < vdim; d += 32) dst_page[d] = src[d];
         return;
     }
     T* row = qkv + (size_t)t * ld + (size_t)(is_q ? g : heads + g) * dim;
     const float* weight = is_q ? q_weight : k_weight;
     float sumsq = 0.f;
-    for (int d = threadIdx.x; d < dim; d += QN_THREADS) {
+    for (int d = lane; d < dim; d += 32) {
         const float v = to_float(row[d]);
         qn_row[d] = v;
         sumsq += v * v;
     }
     if (weight != nullptr) {
-        sumsq = block_sum(sumsq, scratch);
+        sumsq = warp_sum(sumsq);
         const float scale = 1.f / sqrtf(sumsq / (float)dim + eps);
-        for (int d = threadIdx.x; d < dim; d += QN_THREADS) qn_row[d] = qn_row[d] * scale * weight[d];
+        for (int d = lane; d < dim; d += 32) qn_row[d] = qn_row[d] * scale * weight[d];
     }
-    __syncthreads();
+    __syncwarp();
     const int half = rotary_dim / 2;
-    for (int d = threadIdx.x; d < dim; d += QN_THREADS) {
+    for (int d = lane; d < dim; d += 32) {
         float v = qn_row[d];
         if (d < rotary_dim) {
             const int i = d < half ? d : d - half;
@@ -93,9 +96,10 @@ TTB_EXPORT int ttb_qk_norm_rope_write(void* qkv, int dtype, int ld, const int* p
     if (!qkv || !positions || !seg_of_token || !status) return TTB_ERR_ARGUMENT;
     if (write_kv && (!key_pages || !value_pages || !block_table || page_size < 1)) return TTB_ERR_ARGUMENT;
     if (rotary_dim < 0 || (rotary_dim & 1) || rotary_dim > dim || (rotary_dim > 0 && !inv_freq)) return TTB_ERR_ARGUMENT;
-    if (dim < 1 || vdim < 1 || dim > 8192 || heads + 2 * kv_heads > 65535) return TTB_ERR_UNSUPPORTED;
-    dim3 grid(tokens, heads + 2 * kv_heads);
-    const size_t smem = (size_t)dim * sizeof(float);
+    if (dim < 1 || vdim < 1 || heads + 2 * kv_heads > 65535) return TTB_ERR_UNSUPPORTED;
+    dim3 grid(tokens, (heads + 2 * kv_heads + QN_THREADS / 32 - 1) / (QN_THREADS / 32));
+    const size_t smem = (size_t)(QN_THREADS / 32) * dim * sizeof(float);
+    if (smem > 48 * 1024) return TTB_ERR_UNSUPPORTED;
     if (dtype == TTB_DTYPE_BF16)
         ttb_launch(qk_norm_rope_write_kernel<__nv_bfloat16>, grid, QN_THREADS, smem, stream, (__nv_bfloat16*)qkv, ld, positions,
                    seg_of_token, q_weight, k_weight, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, (__nv_bfloat16*)key_pages,

@@ -2,8 +2,8 @@
 //
 // causal_conv: u[t, c] = b_c[c] + sum_j w[c, j] * x(t - taps + 1 + j, c), x(s, c) = round(x'[s, c] + b_x[c]) for tokens of
 //   this step and the request's kept inputs (tail [slots, taps - 1, channels], oldest first; zeros at a request's start)
-//   for positions before it. One thread per (token, channel); nothing is written but u, so that every block sees the
-//   tail as the step before left it.
+//   for positions before it. One thread per (RC_CONV_TOKENS tokens, channel) with the inputs it needs in registers;
+//   nothing is written but u, so that every block sees the tail as the step before left it.
 // gated_recurrence: one thread per (segment, channel) walks the segment's tokens in order:
 //   a = exp(-rate[c] * sigmoid(gr + br));  S = a S + sqrt(1 - a^2) * sigmoid(gi + bi) * u;  out = S * gelu_tanh(y' + b_y)
 //   with the gates' float32 pre-activations [tokens, blocks, 2 s] (decay rows, then input rows, per block). At the end
@@ -17,6 +17,8 @@
 
 #define RC_THREADS 128
 #define RC_MAX_TAPS 16
+#define RC_GROUP 8
+#define RC_CONV_TOKENS 8
 
 __device__ __forceinline__ float rc_gelu_tanh(float z) {
     return 0.5f * z * (1.f + tanhf(0.7978845608028654f * (z + 0.044715f * z * z * z)));
@@ -26,24 +28,32 @@ template <typename T>
 __global__ void __launch_bounds__(RC_THREADS)
 causal_conv_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ bias_x, const float* __restrict__ w,
                    const float* __restrict__ bias_c, const int* __restrict__ seg_of_token, const int* __restrict__ cu_seqlens,
-                   const int* __restrict__ seg_slot, const T* __restrict__ tail, T* __restrict__ u, int channels, int taps) {
+                   const int* __restrict__ seg_slot, const T* __restrict__ tail, T* __restrict__ u, int channels, int taps,
+                   int tokens) {
     pdl_wait();
     pdl_launch_dependents();
-    const int t = blockIdx.y, c = blockIdx.x * RC_THREADS + threadIdx.x;
+    const int c = blockIdx.x * RC_THREADS + threadIdx.x;
     if (c >= channels) return;
-    const int seg = seg_of_token[t];
-    const int start = cu_seqlens[seg];
-    const T* kept = tail + (size_t)seg_slot[seg] * (taps > 1 ? taps - 1 : 1) * channels;
-    const float bx = bias_x[c];
-    float acc = bias_c[c];
-    for (int j = 0; j < taps; ++j) {
-        const int s = t - (taps - 1) + j;                      // flat index of the input this tap reads
-        float v;
-        if (s >= start) v = to_float(from_float<T>(to_float(x[(size_t)s * ldx + c]) + bx));
-        else v = to_float(kept[(size_t)((taps - 1) + (s - start)) * channels + c]);
-        acc = fmaf(w[(size_t)c * taps + j], v, acc);
+    const int first = blockIdx.y * RC_CONV_TOKENS, last = min(first + RC_CONV_TOKENS, tokens);
+    const float bx = bias_x[c], bc = bias_c[c];
+    float w_tap[RC_MAX_TAPS];
+    for (int j = 0; j < taps; ++j) w_tap[j] = w[(size_t)c * taps + j];
+    // the tokens of one group may lie in several segments, so every tap checks its own segment's start; inputs that
+    // neighbouring tokens share come from the first-level cache
+    for (int t = first; t < last; ++t) {
+        const int seg = seg_of_token[t];
+        const int start = cu_seqlens[seg];
+        const T* kept = tail + (size_t)seg_slot[seg] * (taps > 1 ? taps - 1 : 1) * channels;
+        float acc = bc;
+        for (int j = 0; j < taps; ++j) {
+            const int s = t - (taps - 1) + j;                  // flat index of the input this tap reads
+            float v;
+            if (s >= start) v = to_float(from_float<T>(to_float(x[(size_t)s * ldx + c]) + bx));
+            else v = to_float(kept[(size_t)((taps - 1) + (s - start)) * channels + c]);
+            acc = fmaf(w_tap[j], v, acc);
+        }
+        u[(size_t)t * channels + c] = from_float<T>(acc);
     }
-    u[(size_t)t * channels + c] = from_float<T>(acc);
 }
 
 template <typename T>
@@ -78,20 +88,31 @@ gated_recurrence_kernel(const T* __restrict__ u, const float* __restrict__ gates
             S = fmaf(ab[0], S, ab[1]);
         }
     }
-#pragma unroll 4
-    for (int t = t_begin; t < t_end; ++t) {
-        const float gr = gate_r[(size_t)t * gate_ld_token] + br, gi = gate_i[(size_t)t * gate_ld_token] + bi;
-        const float r = 1.f / (1.f + expf(-gr)), in = 1.f / (1.f + expf(-gi));
-        const float log_a = -k * r;
-        const float a = expf(log_a);
-        const float mult = sqrtf(fmaxf(1.f - a * a, 0.f));
-        S = fmaf(a, S, mult * (in * to_float(u[(size_t)t * channels + c])));
-        if (phase == 1) {
-            A *= a;
-            continue;
+    // RC_GROUP tokens at a time: their loads are independent of the recurrence and in flight together
+    for (int t0 = t_begin; t0 < t_end; t0 += RC_GROUP) {
+        float gr[RC_GROUP], gi[RC_GROUP], uu[RC_GROUP], yy[RC_GROUP];
+#pragma unroll
+        for (int k2 = 0; k2 < RC_GROUP; ++k2) {
+            const int t = min(t0 + k2, t_end - 1);
+            gr[k2] = gate_r[(size_t)t * gate_ld_token];
+            gi[k2] = gate_i[(size_t)t * gate_ld_token];
+            uu[k2] = to_float(u[(size_t)t * channels + c]);
+            yy[k2] = phase == 1 ? 0.f : to_float(yx[(size_t)t * ldyx + c]);
         }
-        const float y = rc_gelu_tanh(to_float(yx[(size_t)t * ldyx + c]) + by);
-        out[(size_t)t * channels + c] = from_float<T>(S * y);
+#pragma unroll
+        for (int k2 = 0; k2 < RC_GROUP; ++k2) {
+            const int t = t0 + k2;
+            if (t >= t_end) break;
+            const float r = 1.f / (1.f + expf(-(gr[k2] + br))), in = 1.f / (1.f + expf(-(gi[k2] + bi)));
+            const float a = expf(-k * r);
+            const float mult = sqrtf(fmaxf(1.f - a * a, 0.f));
+            S = fmaf(a, S, mult * (in * uu[k2]));
+            if (phase == 1) {
+                A *= a;
+            } else {
+                out[(size_t)t * channels + c] = from_float<T>(S * rc_gelu_tanh(yy[k2] + by));
+            }
+        }
     }
     if (phase == 1) {
         float* ab = scratch + (((size_t)seg * (parts + 1) + part) * channels + c) * 2;
@@ -124,14 +145,14 @@ TTB_EXPORT int ttb_causal_conv(const void* x, int dtype, int ldx, const float* b
                                int tokens, int channels, int taps, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
     if (!x || !bias_x || !w || !bias_c || !seg_of_token || !cu_seqlens || !seg_slot || !tail || !u) return TTB_ERR_ARGUMENT;
-    if (taps < 1 || taps > RC_MAX_TAPS || channels < 1 || tokens > 65535) return TTB_ERR_UNSUPPORTED;
-    dim3 grid((channels + RC_THREADS - 1) / RC_THREADS, tokens);
+    if (taps < 1 || taps > RC_MAX_TAPS || channels < 1 || tokens > 65535 * RC_CONV_TOKENS) return TTB_ERR_UNSUPPORTED;
+    dim3 grid((channels + RC_THREADS - 1) / RC_THREADS, (tokens + RC_CONV_TOKENS - 1) / RC_CONV_TOKENS);
     if (dtype == TTB_DTYPE_BF16)
         ttb_launch(causal_conv_kernel<__nv_bfloat16>, grid, RC_THREADS, 0, stream, (const __nv_bfloat16*)x, ldx, bias_x, w, bias_c,
-                   seg_of_token, cu_seqlens, seg_slot, (const __nv_bfloat16*)tail, (__nv_bfloat16*)u, channels, taps);
+                   seg_of_token, cu_seqlens, seg_slot, (const __nv_bfloat16*)tail, (__nv_bfloat16*)u, channels, taps, tokens);
     else if (dtype == TTB_DTYPE_F32)
         ttb_launch(causal_conv_kernel<float>, grid, RC_THREADS, 0, stream, (const float*)x, ldx, bias_x, w, bias_c, seg_of_token,
-                   cu_seqlens, seg_slot, (const float*)tail, (float*)u, channels, taps);
+                   cu_seqlens, seg_slot, (const float*)tail, (float*)u, channels, taps, tokens);
     else return TTB_ERR_UNSUPPORTED;
     return ttb_launch_status();
 }

@@ -7,14 +7,13 @@
 //   weight_j = s_j / (sum of the chosen s + floor)
 //
 // Rows whose scores are not numbers (padded rows of a captured step) get scores of zero and choose the first experts.
-// RG_TOKENS tokens a block share one pass over W_r; a warp per logit row, then a warp per token selects. Every logit is
+// RG_TOKENS tokens a block (eight in prompt portions, one in decode steps) share one pass over W_r; a warp per logit row, then a warp per token selects. Every logit is
 // summed in the same order whatever else the batch holds.
 #include "common.cuh"
 
-#define RG_TOKENS 8
 #define RG_MAX_EXPERTS 1024
 
-template <typename T>
+template <typename T, int RG_TOKENS>
 __global__ void __launch_bounds__(512)
 route_grouped_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_router, int width, int experts, int top,
                      int groups, int keep, float floor_, int* __restrict__ choice, float* __restrict__ weight, int tokens) {
@@ -130,21 +129,22 @@ TTB_EXPORT int ttb_route_grouped(const void* x, int dtype, int ldx, const float*
     if (experts < 1 || experts > RG_MAX_EXPERTS || top < 1 || top > experts || groups < 1 || experts % groups || keep < 1 ||
         keep > groups || keep * (experts / groups) < top)
         return TTB_ERR_UNSUPPORTED;
-    const size_t smem = ((size_t)RG_TOKENS * (((width + 3) & ~3) + 2 * experts + groups)) * sizeof(float);
+    const int per_block = tokens > 64 ? 8 : 1;
+    const size_t smem = ((size_t)per_block * (((width + 3) & ~3) + 2 * experts + groups)) * sizeof(float);
     if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
     const int warps = experts < 4 ? 4 : (experts > 16 ? 16 : experts);
-#define RG_LAUNCH(T)                                                                                                  \
+#define RG_LAUNCH(T, N)                                                                                               \
     do {                                                                                                              \
         static TtbOncePerDevice once;                                                                                 \
         if (smem > 48 * 1024 && once.pending()) {                                                                     \
-            cudaFuncSetAttribute(route_grouped_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);   \
+            cudaFuncSetAttribute(route_grouped_kernel<T, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
             once.mark();                                                                                              \
         }                                                                                                             \
-        ttb_launch(route_grouped_kernel<T>, (tokens + RG_TOKENS - 1) / RG_TOKENS, warps * 32, smem, stream, (const T*)x, ldx, \
+        ttb_launch(route_grouped_kernel<T, N>, (tokens + N - 1) / N, warps * 32, smem, stream, (const T*)x, ldx,      \
                    w_router, width, experts, top, groups, keep, floor_, choice, weight, tokens);                      \
     } while (0)
-    if (dtype == TTB_DTYPE_BF16) RG_LAUNCH(__nv_bfloat16);
-    else if (dtype == TTB_DTYPE_F32) RG_LAUNCH(float);
+    if (dtype == TTB_DTYPE_BF16) { if (per_block == 8) RG_LAUNCH(__nv_bfloat16, 8); else RG_LAUNCH(__nv_bfloat16, 1); }
+    else if (dtype == TTB_DTYPE_F32) { if (per_block == 8) RG_LAUNCH(float, 8); else RG_LAUNCH(float, 1); }
     else return TTB_ERR_UNSUPPORTED;
 #undef RG_LAUNCH
     return ttb_launch_status();

@@ -936,6 +936,8 @@ class CudaKernels:
 
     # ------------------------------------------------------------------ recurrent mixers
     RECURRENCE_PART = 64            # tokens of one part of a long segment in the gated recurrence
+    LIGHTNING_PART = 128            # tokens of one part of a long segment in chunked lightning attention (two chunks)
+    LIGHTNING_SCRATCH_BYTES = 256 << 20     # most memory for the parts' states; longer parts beyond it
     LIGHTNING_SCAN_TOKENS = 16      # steps whose longest segment is at most this long walk token by token
 
     def lightning_attention(self, proj, batch, view, heads, dim, vdim, decays, write_state=True):
@@ -949,11 +951,21 @@ class CudaKernels:
         out = torch.empty(tokens, heads * vdim, dtype=torch.float32, device=self.device)
         if (self.use_lightning_chunks and proj.dtype == torch.bfloat16 and batch.max_seg_len > self.LIGHTNING_SCAN_TOKENS
                 and self.lib.ttb_lightning_chunks_supports(dim, vdim)):
-            # prompt portions: chunk by chunk on the tensor cores (decoded tokens and float32 walk token by token)
+            # prompt portions: chunk by chunk on the tensor cores (decoded tokens and float32 walk token by token);
+            # long segments as parts side by side (two launches), as many as their scratch states may take room for
+            part_len, parts, scratch = self.LIGHTNING_PART, 1, None
+            if batch.max_seg_len >= 2 * part_len:
+                per_part = batch.num_segments * heads * dim * vdim * 4
+                while -(-batch.max_seg_len // part_len) * per_part > self.LIGHTNING_SCRATCH_BYTES and part_len < batch.max_seg_len:
+                    part_len *= 2
+                parts = -(-batch.max_seg_len // part_len)
+            if parts > 1:
+                scratch = torch.empty(batch.num_segments * heads * (parts + 1) * dim * vdim, dtype=torch.float32, device=self.device)
+                self.launches += 1
             self._check(self.lib.ttb_lightning_chunks(
                 self._p(proj), proj.stride(0), self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state),
                 self._p(decays), self._p(out), batch.num_segments, heads, dim, vdim, 1 if write_state else 0,
-                self._stream()), "lightning_chunks")
+                self._p(scratch), parts, part_len, self._stream()), "lightning_chunks")
             return out
         self._check(self.lib.ttb_lightning_scan(
             self._p(proj), _dtype_code(proj.dtype), proj.stride(0), self._p(batch.cu_seqlens), self._p(view.slots),
@@ -1090,14 +1102,13 @@ class CudaKernels:
                 self._p(out), code, T, E, top, inter, width, self._stream()), "moe_gemv_plain")
             self.launches += 1
             return out
-        # many pairs: the tokens' rows are laid out expert by expert; the first product leaves float32 rows in that
-        # order (the grouped products write through an index, here 0, 1, 2, ...), the activation rounds them to the
-        # compute dtype, the second product scatters to the pairs' own rows
+        # many pairs: the tokens' rows are laid out expert by expert; the first product leaves the activated hidden rows
+        # in that order (on the fifth-generation tensor cores in its epilogue; on the other paths as float32 rows,
+        # written through the index 0, 1, 2, ..., that an activation kernel rounds to the compute dtype), the second
+        # product scatters to the pairs' own rows
         offsets = torch.empty(E + 1, dtype=torch.int32, device=self.device)
         order = torch.empty(pairs, dtype=torch.int32, device=self.device)
         tokens_of = torch.empty(pairs, dtype=torch.int32, device=self.device)
-        straight = self._iota(pairs)
-        pre = torch.empty(pairs, inter, dtype=torch.float32, device=self.device)
         pair_out = torch.empty(pairs, width, dtype=torch.float32, device=self.device)
         grouped_tc = (x.dtype == torch.bfloat16 and self.use_tcgen05 is not False and pairs >= self.MOE_TCGEN05_PAIRS
                       and width % 8 == 0 and inter % 8 == 0)
@@ -1108,11 +1119,11 @@ class CudaKernels:
                                                self._p(tokens_of), self._p(tile_info[1:]), self._p(tile_info), 128,
                                                self._stream()), "moe_align")
             grouped = self.gather_rows(x, tokens_of)
+            hidden = torch.empty(pairs, inter, dtype=x.dtype, device=self.device)      # the activation in the product's epilogue
             self._check(self.lib.ttb_moe_gemm_tcgen05(
-                self._p(grouped), width, self._p(w_up), width, self._p(pre), inter, 0, self._p(offsets), self._p(straight),
+                self._p(grouped), width, self._p(w_up), width, self._p(hidden), inter, 2, self._p(offsets), self._p(order),
                 self._p(tile_info[1:]), self._p(tile_info), pairs, E, max_tiles, inter, width, ctypes.c_float(0.0),
                 ctypes.c_float(0.0), self._p(self.tc_error), self._stream()), "moe_up_tcgen05")
-            hidden = self.activation(pre, activation, x.dtype)
             self._check(self.lib.ttb_moe_gemm_tcgen05(
                 self._p(hidden), inter, self._p(w_down), inter, self._p(pair_out), width, 0, self._p(offsets), self._p(order),
                 self._p(tile_info[1:]), self._p(tile_info), pairs, E, max_tiles, width, inter, ctypes.c_float(0.0),
@@ -1121,6 +1132,8 @@ class CudaKernels:
             self._check(self.lib.ttb_moe_align(self._p(choice), pairs, E, top, self._p(offsets), self._p(order),
                                                self._p(tokens_of), None, None, 0, self._stream()), "moe_align")
             grouped = self.gather_rows(x, tokens_of)
+            straight = self._iota(pairs)
+            pre = torch.empty(pairs, inter, dtype=torch.float32, device=self.device)
             self._check(self.lib.ttb_moe_group_gemm(
                 self._p(grouped), grouped.stride(0), self._p(w_up), ctypes.c_longlong(inter * width), width, self._p(pre), inter,
                 code, 0, self._p(offsets), self._p(straight), pairs, E, top, inter, width, ctypes.c_float(0.0),
