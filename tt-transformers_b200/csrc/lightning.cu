@@ -116,14 +116,16 @@ TTB_EXPORT int ttb_lightning_scan(const void* proj, int dtype, int ld, const int
 // for the whole segment. A block owns LC_VS columns of one head's state of one segment and walks its chunks in order.
 // Long segments are cut into parts of part_len tokens (a multiple of the chunk) that run side by side (blockIdx.x):
 // the recurrence is linear in S, so in phase 1 every part walks its chunks from S = 0, keys and values only, and leaves
-// its end state in scratch memory; in phase 2 part p starts from S = decay^(p part_len) S_kept + sum_(q<p)
-// decay^((p-1-q) part_len) S_q and walks its chunks again, now with the queries. Phase 0: one part, no scratch.
+// its end state in scratch memory; a small kernel turns the end states into start states, part by part
+// (S_start[0] = the request's kept state, S_start[p + 1] = decay^part_len S_start[p] + S_end[p]); in phase 2 every part
+// walks its chunks again from its start state, now with the queries. Phase 0: one part, no scratch.
 #include <mma.h>
 using namespace nvcuda;
 
 #define LC_C 64
 #define LC_VS 32
 #define LC_THREADS 256
+#define LC_BATCH 8
 
 struct LcLayout {
     int ldq, ldv, lda_f, lda_h, lds_f, lds_h, ldo;
@@ -191,22 +193,15 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
     float* parts_S = scratch + ((size_t)seg * heads + head) * (parts + 1) * dim * vdim;
     const float lambda = decay[head];
     for (int x = tid; x <= LC_C; x += LC_THREADS) pw[x] = x == 0 ? 1.f : powf(lambda, (float)x);
-    const float per_part = phase == 2 ? powf(lambda, (float)part_len) : 1.f;
-    for (int idx = tid; idx < dim * LC_VS; idx += LC_THREADS) {
-        const int d = idx / LC_VS, c = idx % LC_VS;
+    const int lane = tid & 31;
+    for (int d = warp; d < dim; d += LC_THREADS / 32) {
         float v = 0.f;
-        if (c0 + c < vdim) {
-            const size_t at = (size_t)d * vdim + c0 + c;
-            if (phase == 0) {
-                v = S[at];
-            } else if (phase == 1) {
-                if (part == 0) parts_S[(size_t)parts * dim * vdim + at] = S[at];      // kept for phase 2: the last part overwrites S
-            } else {
-                v = parts_S[(size_t)parts * dim * vdim + at];
-                for (int q = 0; q < part; ++q) v = fmaf(per_part, v, parts_S[(size_t)q * dim * vdim + at]);
-            }
+        if (c0 + lane < vdim) {
+            const size_t at = (size_t)d * vdim + c0 + lane;
+            if (phase == 0) v = S[at];
+            else if (phase == 2) v = parts_S[(size_t)part * dim * vdim + at];      // the part's start state (lightning_prefix_kernel)
         }
-        Sf[d * L.lds_f + c] = v;
+        Sf[d * L.lds_f + lane] = v;
     }
     const int q_off = head * dim, k_off = heads * dim + head * dim, v_off = 2 * heads * dim + head * vdim + c0;
     const int d_tiles = dim / 16;
@@ -215,30 +210,56 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
     for (int chunk0 = t_begin; chunk0 < t_end; chunk0 += LC_C) {
         const int n = min(LC_C, t_end - chunk0);
         // ---- the chunk's activations, rounded to bfloat16; rows past the chunk's end are zero; the state in two halves
-        for (int idx = tid; idx < LC_C * dim; idx += LC_THREADS) {
-            const int i = idx / dim, d = idx % dim;
-            float q = 0.f, k = 0.f;
-            if (i < n) {
-                const __nv_bfloat16* row = proj + (size_t)(chunk0 + i) * ld;
-                q = ls_silu(__bfloat162float(row[q_off + d]));
-                k = ls_silu(__bfloat162float(row[k_off + d]));
+        // sixteen bytes (eight values) a load, all loads of a batch in flight before the first is used: a row's q and k
+        // are 2 * dim / 8 such units, a row's LC_VS values four, one unit a thread
+        {
+            const int vi = tid >> 2, vj = tid & 3;
+            uint4 v_raw = make_uint4(0u, 0u, 0u, 0u);
+            if (vi < n && c0 + vj * 8 < vdim) v_raw = *reinterpret_cast<const uint4*>(proj + (size_t)(chunk0 + vi) * ld + v_off + vj * 8);
+            const int q_units = dim >> 3, row_units = dim >> 2, total = LC_C * row_units;
+            for (int base = 0; base < total; base += LC_THREADS * LC_BATCH) {
+                uint4 raw[LC_BATCH];
+#pragma unroll
+                for (int r = 0; r < LC_BATCH; ++r) {
+                    const int u = base + r * LC_THREADS + tid;
+                    raw[r] = make_uint4(0u, 0u, 0u, 0u);
+                    if (u < total) {
+                        const int i = u / row_units, j = u - i * row_units;
+                        const bool is_q = j < q_units;
+                        if (i < n && !(is_q && phase == 1))
+                            raw[r] = *reinterpret_cast<const uint4*>(proj + (size_t)(chunk0 + i) * ld +
+                                                                     (is_q ? q_off + j * 8 : k_off + (j - q_units) * 8));
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < LC_BATCH; ++r) {
+                    const int u = base + r * LC_THREADS + tid;
+                    if (u >= total) continue;
+                    const int i = u / row_units, j = u - i * row_units;
+                    const bool is_q = j < q_units;
+                    float f[8];
+                    const uint32_t w[4] = {raw[r].x, raw[r].y, raw[r].z, raw[r].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        f[2 * e] = ls_silu(__uint_as_float(w[e] << 16));
+                        f[2 * e + 1] = ls_silu(__uint_as_float(w[e] & 0xffff0000u));
+                    }
+                    store8((is_q ? Qs : Ks) + i * L.ldq + (is_q ? j : j - q_units) * 8, f);
+                }
             }
-            Qs[i * L.ldq + d] = __float2bfloat16_rn(q);
-            Ks[i * L.ldq + d] = __float2bfloat16_rn(k);
+            const uint32_t w[4] = {v_raw.x, v_raw.y, v_raw.z, v_raw.w};
+            const float share = vi < n ? pw[n - 1 - vi] : 0.f;       // the value's share of the new state: v_j * decay^(n - 1 - j)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float raw_v = __uint_as_float((e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16));
+                const __nv_bfloat16 vb = __float2bfloat16_rn(ls_silu(raw_v));
+                const int c = vj * 8 + e;
+                Vs[vi * L.ldv + c] = vb;
+                lc_split(__bfloat162float(vb) * share, Vh[vi * L.ldv + c], Vl[vi * L.ldv + c]);
+            }
         }
-        for (int idx = tid; idx < LC_C * LC_VS; idx += LC_THREADS) {
-            const int i = idx / LC_VS, c = idx % LC_VS;
-            float v = 0.f;
-            if (i < n && c0 + c < vdim) v = ls_silu(__bfloat162float(proj[(size_t)(chunk0 + i) * ld + v_off + c]));
-            const __nv_bfloat16 vb = __float2bfloat16_rn(v);
-            Vs[i * L.ldv + c] = vb;
-            // the value's share of the new state: v_j * decay^(n - 1 - j)
-            lc_split(i < n ? __bfloat162float(vb) * pw[n - 1 - i] : 0.f, Vh[i * L.ldv + c], Vl[i * L.ldv + c]);
-        }
-        for (int idx = tid; idx < dim * LC_VS; idx += LC_THREADS) {
-            const int d = idx / LC_VS, c = idx % LC_VS;
-            lc_split(Sf[d * L.lds_f + c], Sh[d * L.lds_h + c], Sl[d * L.lds_h + c]);
-        }
+        for (int d = warp; phase != 1 && d < dim; d += LC_THREADS / 32)
+            lc_split(Sf[d * L.lds_f + lane], Sh[d * L.lds_h + lane], Sl[d * L.lds_h + lane]);
         __syncthreads();
         if (phase != 1) {
         // ---- A = Q K^T (the tiles on and below the diagonal) and Q S0
@@ -274,13 +295,11 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
         }
         __syncthreads();
         // ---- decays, in float32: A'[i, j] = A[i, j] * decay^(i - j) for j <= i, in two halves; (Q S0)[i, :] *= decay^(i + 1)
-        for (int idx = tid; idx < LC_C * LC_C; idx += LC_THREADS) {
-            const int i = idx / LC_C, j = idx % LC_C;
-            lc_split(j <= i ? Af[i * L.lda_f + j] * pw[i - j] : 0.f, Ah[i * L.lda_h + j], Al[i * L.lda_h + j]);
-        }
-        for (int idx = tid; idx < LC_C * LC_VS; idx += LC_THREADS) {
-            const int i = idx / LC_VS, c = idx % LC_VS;
-            Of[i * L.ldo + c] *= pw[i + 1];
+        for (int i = warp; i < LC_C; i += LC_THREADS / 32) {
+#pragma unroll
+            for (int j = lane; j < LC_C; j += 32)
+                lc_split(j <= i ? Af[i * L.lda_f + j] * pw[i - j] : 0.f, Ah[i * L.lda_h + j], Al[i * L.lda_h + j]);
+            Of[i * L.ldo + lane] *= pw[i + 1];
         }
         __syncthreads();
         }
@@ -319,29 +338,45 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
             wmma::store_matrix_sync(Sf + ti * 16 * L.lds_f + tj * 16, acc, L.lds_f, wmma::mem_row_major);
         }
         __syncthreads();
-        for (int idx = tid; phase != 1 && idx < n * LC_VS; idx += LC_THREADS) {
-            const int i = idx / LC_VS, c = idx % LC_VS;
-            if (c0 + c < vdim) out[((size_t)(chunk0 + i) * heads + head) * vdim + c0 + c] = Of[i * L.ldo + c];
-        }
+        for (int i = warp; phase != 1 && i < n; i += LC_THREADS / 32)
+            if (c0 + lane < vdim) out[((size_t)(chunk0 + i) * heads + head) * vdim + c0 + lane] = Of[i * L.ldo + lane];
     }
-    if (phase == 1) {
-        for (int idx = tid; idx < dim * LC_VS; idx += LC_THREADS) {
-            const int d = idx / LC_VS, c = idx % LC_VS;
-            if (c0 + c < vdim) parts_S[(size_t)part * dim * vdim + (size_t)d * vdim + c0 + c] = Sf[d * L.lds_f + c];
-        }
+    if (phase == 1) {                            // the part's end state from a start of zero
+        for (int d = warp; d < dim; d += LC_THREADS / 32)
+            if (c0 + lane < vdim) parts_S[(size_t)part * dim * vdim + (size_t)d * vdim + c0 + lane] = Sf[d * L.lds_f + lane];
         return;
     }
     if (write_state && t_end == seg_end) {
-        for (int idx = tid; idx < dim * LC_VS; idx += LC_THREADS) {
-            const int d = idx / LC_VS, c = idx % LC_VS;
-            if (c0 + c < vdim) S[(size_t)d * vdim + c0 + c] = Sf[d * L.lds_f + c];
-        }
+        for (int d = warp; d < dim; d += LC_THREADS / 32)
+            if (c0 + lane < vdim) S[(size_t)d * vdim + c0 + lane] = Sf[d * L.lds_f + lane];
     }
 }
 
-// The chunked form: bfloat16 projections, dim a multiple of 16 up to 256. Same arguments as ttb_lightning_scan.
+// Between the two phases: scratch[seg, head, p] holds part p's end state from a start of zero and becomes part p's start
+// state: start[0] = the state the request came with, start[p + 1] = decay^part_len * start[p] + end[p]. One thread per
+// element of a head's state walks the parts in order.
+__global__ void lightning_prefix_kernel(float* __restrict__ scratch, const float* __restrict__ state, const int* __restrict__ seg_slot,
+                                        const int* __restrict__ cu_seqlens, const float* __restrict__ decay, int heads,
+                                        int elements, int parts, int part_len) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int e = blockIdx.x * blockDim.x + threadIdx.x, head = blockIdx.y, seg = blockIdx.z;
+    if (e >= elements) return;
+    const int len = cu_seqlens[seg + 1] - cu_seqlens[seg];
+    const int used = (len + part_len - 1) / part_len;           // parts that hold tokens
+    float* mine = scratch + ((size_t)seg * heads + head) * (parts + 1) * elements + e;
+    const float shrink = powf(decay[head], (float)part_len);
+    float start = state[((size_t)seg_slot[seg] * heads + head) * elements + e];
+    for (int p = 0; p < used; ++p) {
+        const float end = mine[(size_t)p * elements];
+        mine[(size_t)p * elements] = start;
+        start = fmaf(shrink, start, end);
+    }
+}
+
+// The chunked form: bfloat16 projections, dim a multiple of 16 up to 256, vdim a multiple of 8, rows of 16-byte alignment. Same arguments as ttb_lightning_scan.
 TTB_EXPORT int ttb_lightning_chunks_supports(int dim, int vdim) {
-    return dim >= 16 && dim <= 256 && (dim & 15) == 0 && vdim >= 1 && lc_layout(dim).total <= 200 * 1024;
+    return dim >= 16 && dim <= 256 && (dim & 15) == 0 && vdim >= 8 && (vdim & 7) == 0 && lc_layout(dim).total <= 200 * 1024;
 }
 
 // parts > 1: scratch holds segments * heads * (parts + 1) * dim * vdim floats, part_len is a multiple of the chunk (64).
@@ -351,6 +386,7 @@ TTB_EXPORT int ttb_lightning_chunks(const void* proj, int ld, const int* cu_seql
     if (segments == 0) return TTB_OK;
     if (!proj || !cu_seqlens || !seg_slot || !state || !decay || !out) return TTB_ERR_ARGUMENT;
     if (!ttb_lightning_chunks_supports(dim, vdim) || heads < 1 || heads > 65535 || segments > 65535) return TTB_ERR_UNSUPPORTED;
+    if ((ld & 7) || !aligned16(proj)) return TTB_ERR_UNSUPPORTED;          // sixteen-byte loads of eight values
     const LcLayout L = lc_layout(dim);
     static TtbOncePerDevice once;
     if (once.pending()) {
@@ -361,8 +397,12 @@ TTB_EXPORT int ttb_lightning_chunks(const void* proj, int ld, const int* cu_seql
     if (L.total > 200 * 1024) return TTB_ERR_UNSUPPORTED;
     if (parts < 1 || (parts > 1 && (!scratch || part_len < LC_C || part_len % LC_C))) return TTB_ERR_ARGUMENT;
     dim3 grid(((vdim + LC_VS - 1) / LC_VS) * parts, heads, segments);
-    for (int phase = parts > 1 ? 1 : 0; phase <= (parts > 1 ? 2 : 0); ++phase)
+    for (int phase = parts > 1 ? 1 : 0; phase <= (parts > 1 ? 2 : 0); ++phase) {
         ttb_launch(lightning_chunk_kernel, grid, LC_THREADS, L.total, stream, (const __nv_bfloat16*)proj, ld, cu_seqlens, seg_slot,
                    state, decay, out, heads, dim, vdim, write_state, scratch, part_len, parts, phase);
+        if (phase == 1)
+            ttb_launch(lightning_prefix_kernel, dim3((dim * vdim + 255) / 256, heads, segments), 256, 0, stream, scratch,
+                       (const float*)state, seg_slot, cu_seqlens, decay, heads, dim * vdim, parts, part_len);
+    }
     return ttb_launch_status();
 }

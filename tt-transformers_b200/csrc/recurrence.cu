@@ -36,21 +36,27 @@ causal_conv_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ b
     if (c >= channels) return;
     const int first = blockIdx.y * RC_CONV_TOKENS, last = min(first + RC_CONV_TOKENS, tokens);
     const float bx = bias_x[c], bc = bias_c[c];
-    float w_tap[RC_MAX_TAPS];
-    for (int j = 0; j < taps; ++j) w_tap[j] = w[(size_t)c * taps + j];
-    // the tokens of one group may lie in several segments, so every tap checks its own segment's start; inputs that
+    const float* w_row = w + (size_t)c * taps;
+    // the tokens of one group may lie in several segments, so every tap checks its own segment's start; a segment's
+    // start, end and slot are looked up again only when the group walks into the next segment; inputs that
     // neighbouring tokens share come from the first-level cache
+    int seg = seg_of_token[first];
+    int start = cu_seqlens[seg], end = cu_seqlens[seg + 1];
+    const T* kept = tail + (size_t)seg_slot[seg] * (taps > 1 ? taps - 1 : 1) * channels;
     for (int t = first; t < last; ++t) {
-        const int seg = seg_of_token[t];
-        const int start = cu_seqlens[seg];
-        const T* kept = tail + (size_t)seg_slot[seg] * (taps > 1 ? taps - 1 : 1) * channels;
+        if (t >= end) {
+            seg = seg_of_token[t];
+            start = cu_seqlens[seg];
+            end = cu_seqlens[seg + 1];
+            kept = tail + (size_t)seg_slot[seg] * (taps > 1 ? taps - 1 : 1) * channels;
+        }
         float acc = bc;
         for (int j = 0; j < taps; ++j) {
             const int s = t - (taps - 1) + j;                  // flat index of the input this tap reads
             float v;
             if (s >= start) v = to_float(from_float<T>(to_float(x[(size_t)s * ldx + c]) + bx));
             else v = to_float(kept[(size_t)((taps - 1) + (s - start)) * channels + c]);
-            acc = fmaf(w_tap[j], v, acc);
+            acc = fmaf(w_row[j], v, acc);
         }
         u[(size_t)t * channels + c] = from_float<T>(acc);
     }

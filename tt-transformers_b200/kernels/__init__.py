@@ -935,7 +935,7 @@ class CudaKernels:
         return out
 
     # ------------------------------------------------------------------ recurrent mixers
-    RECURRENCE_PART = 64            # tokens of one part of a long segment in the gated recurrence
+    RECURRENCE_PART = 16            # tokens of one part of a long segment in the gated recurrence
     LIGHTNING_PART = 128            # tokens of one part of a long segment in chunked lightning attention (two chunks)
     LIGHTNING_SCRATCH_BYTES = 256 << 20     # most memory for the parts' states; longer parts beyond it
     LIGHTNING_SCAN_TOKENS = 16      # steps whose longest segment is at most this long walk token by token
@@ -950,7 +950,7 @@ class CudaKernels:
             raise KernelError("lightning_attention: the state must be float32 [slots, heads, dim, vdim]")
         out = torch.empty(tokens, heads * vdim, dtype=torch.float32, device=self.device)
         if (self.use_lightning_chunks and proj.dtype == torch.bfloat16 and batch.max_seg_len > self.LIGHTNING_SCAN_TOKENS
-                and self.lib.ttb_lightning_chunks_supports(dim, vdim)):
+                and proj.stride(0) % 8 == 0 and proj.data_ptr() % 16 == 0 and self.lib.ttb_lightning_chunks_supports(dim, vdim)):
             # prompt portions: chunk by chunk on the tensor cores (decoded tokens and float32 walk token by token);
             # long segments as parts side by side (two launches), as many as their scratch states may take room for
             part_len, parts, scratch = self.LIGHTNING_PART, 1, None
@@ -998,7 +998,7 @@ class CudaKernels:
         out = torch.empty(tokens, channels, dtype=u.dtype, device=self.device)
         # long segments run as parts of RECURRENCE_PART tokens side by side (two launches: the parts' own products
         # and end states, then the walk that writes out from each part's folded start state)
-        parts = -(-batch.max_seg_len // self.RECURRENCE_PART) if batch.max_seg_len >= 2 * self.RECURRENCE_PART else 1
+        parts = -(-batch.max_seg_len // self.RECURRENCE_PART) if batch.max_seg_len >= 4 * self.RECURRENCE_PART else 1
         scratch = torch.empty(batch.num_segments * (parts + 1) * channels * 2, dtype=torch.float32, device=self.device) if parts > 1 else None
         if parts > 1:
             self.launches += 1
