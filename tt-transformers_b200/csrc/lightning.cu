@@ -86,7 +86,7 @@ TTB_EXPORT int ttb_lightning_scan(const void* proj, int dtype, int ld, const int
                                   cudaStream_t stream) {
     if (segments == 0) return TTB_OK;
     if (!proj || !cu_seqlens || !seg_slot || !state || !decay || !out) return TTB_ERR_ARGUMENT;
-    if (dim < 1 || dim > 256 || vdim < 1 || heads < 1 || heads > 65535 || segments > 65535) return TTB_ERR_UNSUPPORTED;
+    if (dim < 1 || dim > 512 || vdim < 1 || heads < 1 || heads > 65535 || segments > 65535) return TTB_ERR_UNSUPPORTED;
     dim3 grid((vdim + LS_WARPS * LS_COLS - 1) / (LS_WARPS * LS_COLS), heads, segments);
     const int ni = (dim + 31) / 32;
 #define LS_LAUNCH(T, NI)                                                                                              \
@@ -94,7 +94,7 @@ TTB_EXPORT int ttb_lightning_scan(const void* proj, int dtype, int ld, const int
                decay, out, heads, dim, vdim, write_state)
 #define LS_PICK(T)                                                                                                    \
     do {                                                                                                              \
-        if (ni <= 1) LS_LAUNCH(T, 1); else if (ni <= 2) LS_LAUNCH(T, 2); else if (ni <= 4) LS_LAUNCH(T, 4); else LS_LAUNCH(T, 8); \
+        if (ni <= 1) LS_LAUNCH(T, 1); else if (ni <= 2) LS_LAUNCH(T, 2); else if (ni <= 4) LS_LAUNCH(T, 4); else if (ni <= 8) LS_LAUNCH(T, 8); else LS_LAUNCH(T, 16); \
     } while (0)
     if (dtype == TTB_DTYPE_BF16) LS_PICK(__nv_bfloat16);
     else if (dtype == TTB_DTYPE_F32) LS_PICK(float);
@@ -153,6 +153,10 @@ static __host__ __device__ inline LcLayout lc_layout(int dim) {
     L.total = at;
     return L;
 }
+
+// silu for values that are rounded to bfloat16 next: the fast exponential and division (two units in the last place
+// of float32 each) are far below that rounding
+__device__ __forceinline__ float lc_silu(float z) { return __fdividef(z, 1.f + __expf(-z)); }
 
 __device__ __forceinline__ void lc_split(float v, __nv_bfloat16& hi, __nv_bfloat16& lo) {
     hi = __float2bfloat16_rn(v);
@@ -217,6 +221,7 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
             uint4 v_raw = make_uint4(0u, 0u, 0u, 0u);
             if (vi < n && c0 + vj * 8 < vdim) v_raw = *reinterpret_cast<const uint4*>(proj + (size_t)(chunk0 + vi) * ld + v_off + vj * 8);
             const int q_units = dim >> 3, row_units = dim >> 2, total = LC_C * row_units;
+            const int row_shift = (row_units & (row_units - 1)) == 0 ? __ffs(row_units) - 1 : -1;      // a shift where it can be
             for (int base = 0; base < total; base += LC_THREADS * LC_BATCH) {
                 uint4 raw[LC_BATCH];
 #pragma unroll
@@ -224,7 +229,7 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
                     const int u = base + r * LC_THREADS + tid;
                     raw[r] = make_uint4(0u, 0u, 0u, 0u);
                     if (u < total) {
-                        const int i = u / row_units, j = u - i * row_units;
+                        const int i = row_shift >= 0 ? u >> row_shift : u / row_units, j = u - i * row_units;
                         const bool is_q = j < q_units;
                         if (i < n && !(is_q && phase == 1))
                             raw[r] = *reinterpret_cast<const uint4*>(proj + (size_t)(chunk0 + i) * ld +
@@ -235,14 +240,15 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
                 for (int r = 0; r < LC_BATCH; ++r) {
                     const int u = base + r * LC_THREADS + tid;
                     if (u >= total) continue;
-                    const int i = u / row_units, j = u - i * row_units;
+                    const int i = row_shift >= 0 ? u >> row_shift : u / row_units, j = u - i * row_units;
                     const bool is_q = j < q_units;
+                    if (is_q && phase == 1) continue;               // phase 1 walks keys and values only
                     float f[8];
                     const uint32_t w[4] = {raw[r].x, raw[r].y, raw[r].z, raw[r].w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        f[2 * e] = ls_silu(__uint_as_float(w[e] << 16));
-                        f[2 * e + 1] = ls_silu(__uint_as_float(w[e] & 0xffff0000u));
+                        f[2 * e] = lc_silu(__uint_as_float(w[e] << 16));
+                        f[2 * e + 1] = lc_silu(__uint_as_float(w[e] & 0xffff0000u));
                     }
                     store8((is_q ? Qs : Ks) + i * L.ldq + (is_q ? j : j - q_units) * 8, f);
                 }
@@ -252,7 +258,7 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
                 const float raw_v = __uint_as_float((e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16));
-                const __nv_bfloat16 vb = __float2bfloat16_rn(ls_silu(raw_v));
+                const __nv_bfloat16 vb = __float2bfloat16_rn(lc_silu(raw_v));
                 const int c = vj * 8 + e;
                 Vs[vi * L.ldv + c] = vb;
                 lc_split(__bfloat162float(vb) * share, Vh[vi * L.ldv + c], Vl[vi * L.ldv + c]);
@@ -261,6 +267,26 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
         for (int d = warp; phase != 1 && d < dim; d += LC_THREADS / 32)
             lc_split(Sf[d * L.lds_f + lane], Sh[d * L.lds_h + lane], Sl[d * L.lds_h + lane]);
         __syncthreads();
+        // ---- S = decay^n S + K^T V' (it reads the old state, whose two halves Q S0 below reads from their own copies;
+        //      the warps take its tiles from the last warp down, the query products from the first warp up)
+        const float shrink = pw[n];
+        for (int tile = LC_THREADS / 32 - 1 - warp; tile < d_tiles * (LC_VS / 16); tile += LC_THREADS / 32) {
+            const int ti = tile / (LC_VS / 16), tj = tile % (LC_VS / 16);
+            wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
+            wmma::load_matrix_sync(acc, Sf + ti * 16 * L.lds_f + tj * 16, L.lds_f, wmma::mem_row_major);
+#pragma unroll
+            for (int e = 0; e < acc.num_elements; ++e) acc.x[e] *= shrink;
+            for (int kk = 0; kk < LC_C / 16; ++kk) {
+                wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::col_major> a;     // K^T: element (d, j) = K[j][d]
+                wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::row_major> b;
+                wmma::load_matrix_sync(a, Ks + kk * 16 * L.ldq + ti * 16, L.ldq);
+                wmma::load_matrix_sync(b, Vh + kk * 16 * L.ldv + tj * 16, L.ldv);
+                wmma::mma_sync(acc, a, b, acc);
+                wmma::load_matrix_sync(b, Vl + kk * 16 * L.ldv + tj * 16, L.ldv);
+                wmma::mma_sync(acc, a, b, acc);
+            }
+            wmma::store_matrix_sync(Sf + ti * 16 * L.lds_f + tj * 16, acc, L.lds_f, wmma::mem_row_major);
+        }
         if (phase != 1) {
         // ---- A = Q K^T (the tiles on and below the diagonal) and Q S0
         for (int tile = warp; tile < (LC_C / 16) * (LC_C / 16); tile += LC_THREADS / 32) {
@@ -303,7 +329,7 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
         }
         __syncthreads();
         }
-        // ---- O += A' V;  S = decay^n S + K^T V'
+        // ---- O += A' V
         for (int tile = warp; phase != 1 && tile < (LC_C / 16) * (LC_VS / 16); tile += LC_THREADS / 32) {
             const int ti = tile / (LC_VS / 16), tj = tile % (LC_VS / 16);
             wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
@@ -318,24 +344,6 @@ lightning_chunk_kernel(const __nv_bfloat16* __restrict__ proj, int ld, const int
                 wmma::mma_sync(acc, a, b, acc);
             }
             wmma::store_matrix_sync(Of + ti * 16 * L.ldo + tj * 16, acc, L.ldo, wmma::mem_row_major);
-        }
-        const float shrink = pw[n];
-        for (int tile = warp; tile < d_tiles * (LC_VS / 16); tile += LC_THREADS / 32) {
-            const int ti = tile / (LC_VS / 16), tj = tile % (LC_VS / 16);
-            wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
-            wmma::load_matrix_sync(acc, Sf + ti * 16 * L.lds_f + tj * 16, L.lds_f, wmma::mem_row_major);
-#pragma unroll
-            for (int e = 0; e < acc.num_elements; ++e) acc.x[e] *= shrink;
-            for (int kk = 0; kk < LC_C / 16; ++kk) {
-                wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::col_major> a;     // K^T: element (d, j) = K[j][d]
-                wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::row_major> b;
-                wmma::load_matrix_sync(a, Ks + kk * 16 * L.ldq + ti * 16, L.ldq);
-                wmma::load_matrix_sync(b, Vh + kk * 16 * L.ldv + tj * 16, L.ldv);
-                wmma::mma_sync(acc, a, b, acc);
-                wmma::load_matrix_sync(b, Vl + kk * 16 * L.ldv + tj * 16, L.ldv);
-                wmma::mma_sync(acc, a, b, acc);
-            }
-            wmma::store_matrix_sync(Sf + ti * 16 * L.lds_f + tj * 16, acc, L.lds_f, wmma::mem_row_major);
         }
         __syncthreads();
         for (int i = warp; phase != 1 && i < n; i += LC_THREADS / 32)
