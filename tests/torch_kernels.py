@@ -338,6 +338,12 @@ class TorchKernels:
             start += n
         return out.to(u.dtype)
 
+    def recurrent_token(self, yx, bias_yx, conv_w, conv_b, w_gates, gate_bias, rate, batch, view, write_state=True):
+        C, B = yx.shape[1] // 2, w_gates.shape[0]
+        u = self.causal_conv(yx[:, C:], bias_yx[C:], conv_w, conv_b, batch, view)
+        gates = self.heads_linear(u.view(-1, B, C // B), w_gates, out_dtype=torch.float32)
+        return self.gated_recurrence(u, gates, gate_bias, rate, yx, bias_yx, batch, view, write_state)
+
     # ------------------------------------------------------------------ attention with a sink, a cap, chunks
     def qk_norm_rope_write(self, qkv, batch, q_norm, k_norm, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, view,
                            write_kv=True):

@@ -191,3 +191,92 @@ TTB_EXPORT int ttb_gated_recurrence(const void* u, int dtype, const float* gates
     }
     return ttb_launch_status();
 }
+
+// ---------------------------------------------------------------- a decoded token: convolution, gates and recurrence in one kernel
+// Every segment holds one token. A block owns one block of channels of one segment: its threads compute the
+// convolution's output u for their channels (rounded to the compute type, as the kernels above hand it on) into shared
+// memory and shift the kept inputs, its warps then sum the 2 s gate rows of the block's matrix against u in float32, and
+// its threads walk the recurrence one step and write S * gelu_tanh(y).
+#define RT_THREADS 256
+
+template <typename T>
+__global__ void __launch_bounds__(RT_THREADS)
+recurrent_token_kernel(const T* __restrict__ yx, int ldyx, const float* __restrict__ bias_yx, const float* __restrict__ conv_w,
+                       const float* __restrict__ conv_b, const T* __restrict__ w_gates, const float* __restrict__ gate_bias,
+                       const float* __restrict__ rate, const int* __restrict__ cu_seqlens, const int* __restrict__ seg_slot,
+                       float* __restrict__ state, T* __restrict__ tail, T* __restrict__ out, int channels, int block_size, int taps,
+                       int write_state) {
+    extern __shared__ float rt_smem[];
+    float* u_s = rt_smem;                     // [block_size]
+    float* g_s = rt_smem + block_size;        // [2 block_size]
+    const int seg = blockIdx.y, b = blockIdx.x;
+    const T* w_block = w_gates + (size_t)b * 2 * block_size * block_size;
+    for (size_t off = (size_t)threadIdx.x * 128; off < (size_t)2 * block_size * block_size * sizeof(T); off += (size_t)RT_THREADS * 128)
+        prefetch_l2(reinterpret_cast<const char*>(w_block) + off);      // weights: nobody writes them
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t = cu_seqlens[seg];
+    if (cu_seqlens[seg + 1] <= t) return;
+    const int slot = seg_slot[seg];
+    const int keep = taps - 1;
+    for (int i = threadIdx.x; i < block_size; i += RT_THREADS) {
+        const int c = b * block_size + i;
+        const float fresh = to_float(from_float<T>(to_float(yx[(size_t)t * ldyx + channels + c]) + bias_yx[channels + c]));
+        T* kept = tail + (size_t)slot * (keep > 0 ? keep : 1) * channels;
+        float window[RC_MAX_TAPS];
+        for (int j = 0; j < keep; ++j) window[j] = to_float(kept[(size_t)j * channels + c]);
+        float acc = conv_b[c];
+        for (int j = 0; j < keep; ++j) acc = fmaf(conv_w[(size_t)c * taps + j], window[j], acc);
+        acc = fmaf(conv_w[(size_t)c * taps + keep], fresh, acc);
+        u_s[i] = to_float(from_float<T>(acc));
+        if (write_state) {
+            for (int j = 0; j + 1 < keep; ++j) kept[(size_t)j * channels + c] = from_float<T>(window[j + 1]);
+            if (keep > 0) kept[(size_t)(keep - 1) * channels + c] = from_float<T>(fresh);
+        }
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int o = warp; o < 2 * block_size; o += RT_THREADS / 32) {
+        const T* row = w_block + (size_t)o * block_size;
+        float sum = 0.f;
+        for (int k = lane; k < block_size; k += 32) sum = fmaf(to_float(row[k]), u_s[k], sum);
+        sum = warp_sum(sum);
+        if (lane == 0) g_s[o] = sum;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < block_size; i += RT_THREADS) {
+        const int c = b * block_size + i;
+        const float gr = g_s[i] + gate_bias[(size_t)b * 2 * block_size + i];
+        const float gi = g_s[block_size + i] + gate_bias[(size_t)b * 2 * block_size + block_size + i];
+        const float r = 1.f / (1.f + expf(-gr)), in = 1.f / (1.f + expf(-gi));
+        const float a = expf(-rate[c] * r);
+        const float S = fmaf(a, state[(size_t)slot * channels + c], sqrtf(fmaxf(1.f - a * a, 0.f)) * (in * u_s[i]));
+        out[(size_t)t * channels + c] = from_float<T>(S * rc_gelu_tanh(to_float(yx[(size_t)t * ldyx + c]) + bias_yx[c]));
+        if (write_state) state[(size_t)slot * channels + c] = S;
+    }
+}
+
+// yx [tokens, ldyx] as for ttb_gated_recurrence; w_gates [blocks, 2 s, s] of the compute type; every segment holds one token.
+TTB_EXPORT int ttb_recurrent_token(const void* yx, int dtype, int ldyx, const float* bias_yx, const float* conv_w, const float* conv_b,
+                                   const void* w_gates, const float* gate_bias, const float* rate, const int* cu_seqlens,
+                                   const int* seg_slot, float* state, void* tail, void* out, int segments, int channels, int blocks,
+                                   int taps, int write_state, cudaStream_t stream) {
+    if (segments == 0) return TTB_OK;
+    if (!yx || !bias_yx || !conv_w || !conv_b || !w_gates || !gate_bias || !rate || !cu_seqlens || !seg_slot || !state || !tail || !out)
+        return TTB_ERR_ARGUMENT;
+    if (taps < 1 || taps > RC_MAX_TAPS || blocks < 1 || channels % blocks || segments > 65535 || blocks > 65535) return TTB_ERR_UNSUPPORTED;
+    const int s = channels / blocks;
+    const size_t smem = (size_t)3 * s * sizeof(float);
+    if (smem > 48 * 1024) return TTB_ERR_UNSUPPORTED;
+    dim3 grid(blocks, segments);
+    if (dtype == TTB_DTYPE_BF16)
+        ttb_launch(recurrent_token_kernel<__nv_bfloat16>, grid, RT_THREADS, smem, stream, (const __nv_bfloat16*)yx, ldyx, bias_yx, conv_w,
+                   conv_b, (const __nv_bfloat16*)w_gates, gate_bias, rate, cu_seqlens, seg_slot, state, (__nv_bfloat16*)tail,
+                   (__nv_bfloat16*)out, channels, s, taps, write_state);
+    else if (dtype == TTB_DTYPE_F32)
+        ttb_launch(recurrent_token_kernel<float>, grid, RT_THREADS, smem, stream, (const float*)yx, ldyx, bias_yx, conv_w, conv_b,
+                   (const float*)w_gates, gate_bias, rate, cu_seqlens, seg_slot, state, (float*)tail, (float*)out, channels, s, taps,
+                   write_state);
+    else return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}

@@ -8,7 +8,8 @@
 //
 // Rows whose scores are not numbers (padded rows of a captured step) get scores of zero and choose the first experts.
 // RG_TOKENS tokens a block (eight in prompt portions, one in decode steps) share one pass over W_r; a warp per logit row, then a warp per token selects. Every logit is
-// summed in the same order whatever else the batch holds.
+// summed in the same order whatever else the batch holds (a lane takes four neighbouring columns at a time where the width
+// allows 16-byte loads, in prompt portions and in decode steps alike).
 #include "common.cuh"
 
 #define RG_MAX_EXPERTS 1024
@@ -23,6 +24,12 @@ route_grouped_kernel(const T* __restrict__ x, int ldx, const float* __restrict__
     float* z = h + RG_TOKENS * wpad;                      // [RG_TOKENS, experts]: logits, then scores
     int* open = reinterpret_cast<int*>(z + RG_TOKENS * experts);     // [RG_TOKENS, experts]: 1 while an expert may be chosen
     float* gbest = reinterpret_cast<float*>(open + RG_TOKENS * experts);     // [RG_TOKENS, groups]
+    if (RG_TOKENS == 1) {      // a handful of tokens: the router's matrix on its way into L2 while the norm in front finishes
+        const char* w = reinterpret_cast<const char*>(w_router);
+        const size_t bytes = (size_t)experts * width * sizeof(float);
+        for (size_t off = (size_t)(blockIdx.x * blockDim.x + threadIdx.x) * 128; off < bytes; off += (size_t)gridDim.x * blockDim.x * 128)
+            prefetch_l2(w + off);
+    }
     pdl_wait();
     pdl_launch_dependents();
     const int t0 = blockIdx.x * RG_TOKENS, nt = min(RG_TOKENS, tokens - t0);
@@ -31,15 +38,28 @@ route_grouped_kernel(const T* __restrict__ x, int ldx, const float* __restrict__
             h[i * wpad + c] = (i < nt && c < width) ? to_float(x[(size_t)(t0 + i) * ldx + c]) : 0.f;
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const bool vec = (width & 3) == 0 && (reinterpret_cast<uintptr_t>(w_router) & 15) == 0;
     for (int e = warp; e < experts; e += nwarps) {
         const float* w = w_router + (size_t)e * width;
         float s[RG_TOKENS];
 #pragma unroll
         for (int i = 0; i < RG_TOKENS; ++i) s[i] = 0.f;
-        for (int c = lane; c < width; c += 32) {
-            const float a = w[c];
+        if (vec) {          // a lane's loads are independent of one another: they are in flight together
+#pragma unroll 4
+            for (int c = lane * 4; c < width; c += 128) {
+                const float4 a = *reinterpret_cast<const float4*>(w + c);
 #pragma unroll
-            for (int i = 0; i < RG_TOKENS; ++i) s[i] = fmaf(h[i * wpad + c], a, s[i]);
+                for (int i = 0; i < RG_TOKENS; ++i) {
+                    const float4 x4 = *reinterpret_cast<const float4*>(h + i * wpad + c);
+                    s[i] = fmaf(a.x, x4.x, s[i]); s[i] = fmaf(a.y, x4.y, s[i]); s[i] = fmaf(a.z, x4.z, s[i]); s[i] = fmaf(a.w, x4.w, s[i]);
+                }
+            }
+        } else {
+            for (int c = lane; c < width; c += 32) {
+                const float a = w[c];
+#pragma unroll
+                for (int i = 0; i < RG_TOKENS; ++i) s[i] = fmaf(h[i * wpad + c], a, s[i]);
+            }
         }
 #pragma unroll
         for (int i = 0; i < RG_TOKENS; ++i) {

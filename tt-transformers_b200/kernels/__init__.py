@@ -100,7 +100,8 @@ class CudaKernels:
                      "ttb_latent_attention_mma_tokens_per_tile", "ttb_stream_add_norm", "ttb_gated_rmsnorm",
                      "ttb_mean_rmsnorm_pair", "ttb_activation", "ttb_lightning_scan", "ttb_causal_conv", "ttb_gated_recurrence",
                      "ttb_paged_attention_generic_ext", "ttb_qk_norm_rope_write", "ttb_route_grouped", "ttb_moe_gemv_plain",
-                     "ttb_paged_attention_mma_ext", "ttb_lightning_chunks", "ttb_lightning_chunks_supports"):
+                     "ttb_paged_attention_mma_ext", "ttb_lightning_chunks", "ttb_lightning_chunks_supports",
+                     "ttb_recurrent_token"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -1010,14 +1011,30 @@ class CudaKernels:
             self.RECURRENCE_PART, self._stream()), "gated_recurrence")
         return out
 
+    def recurrent_token(self, yx, bias_yx, conv_w, conv_b, w_gates, gate_bias, rate, batch, view, write_state=True):
+        """causal_conv, the gates' block products and gated_recurrence for a step in which every segment holds one
+        token, in one kernel. yx [T, y | x'] before their biases; w_gates [blocks, 2 s, s]. -> [T, channels]."""
+        tokens, two = yx.shape
+        channels, blocks = two // 2, w_gates.shape[0]
+        if (yx.stride(1) != 1 or w_gates.dtype != yx.dtype or not w_gates.is_contiguous() or view.tail.dtype != yx.dtype
+                or batch.max_seg_len != 1):
+            raise KernelError("recurrent_token: one token per segment, weights and kept inputs of the compute dtype")
+        out = torch.empty(tokens, channels, dtype=yx.dtype, device=self.device)
+        self._check(self.lib.ttb_recurrent_token(
+            self._p(yx), _dtype_code(yx.dtype), yx.stride(0), self._p(bias_yx), self._p(conv_w), self._p(conv_b),
+            self._p(w_gates), self._p(gate_bias), self._p(rate), self._p(batch.cu_seqlens), self._p(view.slots),
+            self._p(view.state), self._p(view.tail), self._p(out), batch.num_segments, channels, blocks, view.taps,
+            1 if write_state else 0, self._stream()), "recurrent_token")
+        return out
+
     # ------------------------------------------------------------------ attention with a sink, a cap, chunks
     def qk_norm_rope_write(self, qkv, batch, q_norm, k_norm, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, view,
                            write_kv=True):
         """In place on qkv [T, heads * dim | kv_heads * dim | kv_heads * vdim]: RMS norm per head of q and k (weights
         float32 [dim] or None), rotation of their first rotary_dim elements; keys and values go into their pages."""
         tokens = qkv.shape[0]
-        if qkv.shape[1] != (heads + kv_heads) * dim + kv_heads * vdim or not qkv.is_contiguous():
-            raise KernelError("qk_norm_rope_write: qkv must be contiguous [tokens, heads * dim + kv_heads * (dim + vdim)]")
+        if qkv.shape[1] != (heads + kv_heads) * dim + kv_heads * vdim or qkv.stride(1) != 1:
+            raise KernelError("qk_norm_rope_write: qkv must be [tokens, heads * dim + kv_heads * (dim + vdim)], contiguous along its columns")
         if (q_norm is None) != (k_norm is None):
             raise KernelError("qk_norm_rope_write: both norms or none")
         write = bool(write_kv and view is not None)
@@ -1039,7 +1056,7 @@ class CudaKernels:
             raise KernelError("sink_attention: cache pages and queries differ in dtype")
         out = torch.empty(tokens, heads * vdim, dtype=qkv.dtype, device=self.device)
         if (self.use_mma_attention and qkv.dtype == torch.bfloat16 and dim == vdim and qkv.stride(0) % 8 == 0
-                and view.keys.is_contiguous() and view.values.is_contiguous()
+                and qkv.data_ptr() % 16 == 0 and view.keys.is_contiguous() and view.values.is_contiguous()
                 and self.lib.ttb_attention_mma_supports(heads, kv_heads, dim)):
             # keys and values of one size that the tensor-core kernel takes: 64-row tiles for prompt portions, the
             # decode shape for single tokens; key splits sized by what a query can see at most

@@ -59,10 +59,23 @@ class GatedRecurrence(Mixer):
     def cache_request(self):
         return RecurrentState(self.channels, self.taps)
 
-    def forward(self, x, batch, cache, write_cache=True):
+    @property
+    def input_weight(self):
+        return self.w_in
+
+    @input_weight.setter
+    def input_weight(self, rows):
+        self.w_in = rows
+
+    def forward(self, x, batch, cache, write_cache=True, projected=None):
         k = self.runtime.kernels
         C, B = self.channels, self.blocks
-        yx = k.linear(x, self.w_in)                                            # [T, y | x'] without their biases
+        yx = projected if projected is not None else k.linear(x, self.w_in)                                            # [T, y | x'] without their biases
+        if batch.max_seg_len == 1 and (C // B) * 12 <= 48 * 1024:
+            # decoded tokens: convolution, gates and recurrence in one kernel
+            mixed = k.recurrent_token(yx, self.b_in, self.conv, self.conv_b, self.w_gates, self.b_gates, self.rate, batch, cache,
+                                      write_cache)
+            return k.linear(mixed, self.w_o)
         u = k.causal_conv(yx[:, C:], self.b_in[C:], self.conv, self.conv_b, batch, cache)          # [T, C]
         gates = k.heads_linear(u.view(-1, B, C // B), self.w_gates, out_dtype=torch.float32)      # [T, B, 2 s]
         mixed = k.gated_recurrence(u, gates, self.b_gates, self.rate, yx, self.b_in, batch, cache, write_cache)

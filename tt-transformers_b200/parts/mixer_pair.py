@@ -42,6 +42,15 @@ class MixerPair(Mixer):
         f32 = dict(device=runtime.device, dtype=torch.float32)
         self.w_left = tensors[self.left_norm].to(**f32).contiguous()
         self.w_right = tensors[self.right_norm].to(**f32).contiguous()
+        # both mixers project the same input: where both say which rows they need, one product serves them
+        self.w_both = None
+        if all(hasattr(m, "input_weight") for m in (self.left, self.right)):
+            a, b = self.left.input_weight, self.right.input_weight
+            if a.dtype == b.dtype and a.shape[1] == b.shape[1] and a.shape[0] % 8 == 0:
+                self.w_both = torch.cat([a, b], 0).contiguous()
+                self.rows_left = a.shape[0]
+                self.left.input_weight = self.w_both[:self.rows_left]          # the same storage, not a second copy
+                self.right.input_weight = self.w_both[self.rows_left:]
 
     def cache_request(self):
         kept = tuple(r for r in self._requests if r is not None)
@@ -61,9 +70,16 @@ class MixerPair(Mixer):
     def forward(self, x, batch, cache, write_cache=True):
         views = iter(cache or ())
         outs = []
-        for m, request in zip((self.left, self.right), self._requests):
+        slices = (None, None)
+        if self.w_both is not None:
+            both = self.runtime.kernels.linear(x, self.w_both)
+            slices = (both[:, :self.rows_left], both[:, self.rows_left:])
+        for m, request, projected in zip((self.left, self.right), self._requests, slices):
             view = next(views) if request is not None else None
-            outs.append(m.forward(x, batch, view, write_cache))
+            if projected is not None:
+                outs.append(m.forward(x, batch, view, write_cache, projected=projected))
+            else:
+                outs.append(m.forward(x, batch, view, write_cache))
         return self.runtime.kernels.mean_rmsnorm_pair(outs[0], self.w_left, outs[1], self.w_right, self.eps)
 
 

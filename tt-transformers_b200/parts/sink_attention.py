@@ -75,11 +75,21 @@ class SinkAttention(Mixer):
         step's metadata in its one copy to the device)."""
         return self.runtime.kernels.attention_tables(seg_lens, seg_pos0, self.heads // self.kv_heads, fixed_tokens)
 
-    def forward(self, x, batch, cache, write_cache=True):
+    # a mixer that stands beside another one may get its input projection as a slice of one product for both:
+    # `input_weight` is what that product needs of this mixer, `projected` what comes back
+    @property
+    def input_weight(self):
+        return self.w_qkv
+
+    @input_weight.setter
+    def input_weight(self, rows):
+        self.w_qkv = rows
+
+    def forward(self, x, batch, cache, write_cache=True, projected=None):
         k = self.runtime.kernels
         rotation = self.position.rotation() if self.position is not None else None
         inv_freq, rotary_dim = rotation if rotation is not None else (None, 0)
-        qkv = k.linear(x, self.w_qkv)
+        qkv = projected if projected is not None else k.linear(x, self.w_qkv)
         k.qk_norm_rope_write(qkv, batch, self.q_norm, self.k_norm, self.eps, inv_freq, rotary_dim, self.heads,
                              self.kv_heads, self.dim, self.vdim, cache, write_cache)
         mixed = k.sink_attention(qkv, batch, self.heads, self.kv_heads, self.dim, self.vdim, self.scale, self.softcap,
