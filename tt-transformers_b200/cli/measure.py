@@ -548,7 +548,7 @@ class KernelTimer:
 _TIMED = {"Bozavik": ["add_layernorm", "latent_prepare", "heads_linear", "_latent_attention", "latent_out", "gate_heads", "route_top",
                       "routed_experts", "linear"],
           "Pedazen": ["stream_add_norm", "lightning_attention", "gated_rmsnorm", "qk_norm_rope_write", "sink_attention",
-                      "causal_conv", "heads_linear", "gated_recurrence", "mean_rmsnorm_pair", "route_grouped", "plain_experts",
+                      "causal_conv", "heads_linear", "gated_recurrence", "recurrent_token", "mean_rmsnorm_pair", "route_grouped", "plain_experts",
                       "glu_activation", "linear"],
           "Llama": ["add_rmsnorm", "rope_kv_write", "fused_qkv_rope", "paged_attention", "linear_swiglu", "linear"]}
 
