@@ -65,6 +65,14 @@ PLAIN = config(64, 200, [
 ], loop=None)
 
 
+# head sizes that the tensor-core kernels take (attention with keys and values of 64, linear attention in chunks), chunks
+# that end inside a key tile, a loop over both layers
+TENSOR = config(128, 260, [
+    layer(parallel(4, 2, 64, 64, chunk=40, rot_dims=32, channels=128, blocks=2, taps=4, softcap=15.0), moe(6, 2, 64, count=3, keep=2)),
+    layer(lightning(2, 64, 64, (0.98, 0.7)), dense(192)),
+], loop=(0, 2, 2))
+
+
 def single(kind):
     """One layer with one mechanism and nothing beside it."""
     if kind == "lightning":

@@ -275,6 +275,25 @@ def test_sink_attention_against_its_twin(kernels, twin, dtype, heads, kv_heads, 
     assert float((more.float() - got.float()).abs().max()) > 0.02          # a sink that is left out shows
 
 
+@pytest.mark.parametrize("heads,kv_heads,dim,page,chunk", [(8, 2, 64, 16, None), (4, 1, 128, 16, 600), (6, 3, 64, 32, 256), (2, 2, 128, 16, 1024)])
+def test_sink_attention_over_long_contexts_with_key_splits(kernels, twin, heads, kv_heads, dim, page, chunk):
+    """Contexts long enough for the tensor-core kernel to cut a query's keys into splits that are merged afterwards:
+    the sink joins the denominator once, whichever split holds it; decoded tokens and prompt portions."""
+    for segs in ([(1100, 1), (700, 1)], [(0, 700)], [(600, 3), (511, 2), (1023, 1), (1024, 1)]):
+        batch, view, qkv, g = _attention_setup(segs, heads, kv_heads, dim, dim, page, chunk, None, torch.bfloat16, seed=dim + len(segs))
+        sinks = (torch.randn(heads, generator=g) * 2 + 2).to(DEV)
+        twin.qk_norm_rope_write(qkv, batch, None, None, 1e-5, None, 0, heads, kv_heads, dim, dim, view)
+        for cap, use_sinks in ((25.0, sinks), (None, None)):
+            ref = twin.sink_attention(qkv, batch, heads, kv_heads, dim, dim, 0.2, cap, use_sinks, view)
+            got = kernels.sink_attention(qkv, batch, heads, kv_heads, dim, dim, 0.2, cap, use_sinks, view)
+            _close(got, ref, 2e-2)
+            kernels.use_mma_attention = False                   # the float32-arithmetic kernel on the same pages
+            try:
+                _close(kernels.sink_attention(qkv, batch, heads, kv_heads, dim, dim, 0.2, cap, use_sinks, view), ref, 2e-2)
+            finally:
+                kernels.use_mma_attention = True
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_one_key_carries_the_weight_inside_its_chunk_only(kernels, dtype):
     check_one_key_carries_the_weight(kernels, DEV, dtype)
@@ -314,7 +333,7 @@ def _plain(cfg, w, toks):
 
 
 @pytest.mark.parametrize("dtype,tol", [("float32", 1e-4), ("bfloat16", 6e-2)])
-@pytest.mark.parametrize("name", ["ALIGNED", "ODD", "PLAIN"])
+@pytest.mark.parametrize("name", ["ALIGNED", "ODD", "PLAIN", "TENSOR"])
 def test_engine_matches_the_plain_implementation(tmp_path, dtype, tol, name):
     folder = cases.write_folder(str(tmp_path / name), getattr(cases, name), seed=3,
                                 dtype=torch.float32 if dtype == "float32" else torch.bfloat16)
